@@ -1,0 +1,202 @@
+/*
+ * nie_b200.h - C ABI of the B200 (sm_100a) ragged-batch attention path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * passed as `void*` (NULL = legacy default stream).  No torch or C++ types
+ * cross this boundary, so the library can be bound from ctypes, cffi, cgo or
+ * JNI alike.  All pointers are DEVICE pointers unless stated otherwise.
+ *
+ * Cache layout (identical to the reference's PagedKVCache storage,
+ * nano_infer_engine/paged_cache.py:131-139):
+ *     key_cache / value_cache : [num_layers, num_blocks, block_size,
+ *                                kv_heads, head_dim], contiguous
+ * A "slot" is block_id * block_size + offset_in_block
+ * (nano_infer_engine/paged_cache.py:313-322).
+ *
+ * Return value: NIE_OK (0) or an NIE_ERR_* code; nie_last_error() gives the
+ * message of the last failure on the calling thread.  Launches are
+ * asynchronous; device-side range violations (a block id outside the pool, a
+ * slot outside the cache) never trap: the kernel skips the access and ORs an
+ * NIE_DEV_ERR_* bit into the optional `err_flag` word (int32, device).
+ */
+#ifndef NIE_B200_H
+#define NIE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types of q / k / v / caches */
+#define NIE_DTYPE_F32 0
+#define NIE_DTYPE_BF16 1
+#define NIE_DTYPE_F16 2
+
+/* host-side status codes */
+#define NIE_OK 0
+#define NIE_ERR_INVALID 1     /* bad argument (shape, pointer, range) */
+#define NIE_ERR_UNSUPPORTED 2 /* valid but not implemented for this shape */
+#define NIE_ERR_CUDA 3        /* a CUDA runtime/driver call failed */
+
+/* device-side error bits (ORed into *err_flag) */
+#define NIE_DEV_ERR_BLOCK_RANGE 1 /* block table entry outside [0, num_blocks) */
+#define NIE_DEV_ERR_SLOT_RANGE 2  /* slot outside [0, num_blocks*block_size) */
+#define NIE_DEV_ERR_TIMEOUT 4     /* a bounded wait on an mbarrier ran out */
+#define NIE_DEV_ERR_CAPACITY 8    /* position beyond the block table row */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int nie_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* nie_last_error(void);
+
+/* Number of SMs of `device` (cached); <0 on error. */
+int nie_device_sm_count(int device);
+
+/*
+ * (a) Ragged batch packing.
+ * Replaces the host-side packing of the reference:
+ *   query_start_loc      nano_infer_engine/generation/paged_prefill.py:132-143
+ *   position ids         nano_infer_engine/layers/attention.py:539-550
+ *   context lengths      nano_infer_engine/models/llama.py:364-369
+ *   slot resolution      nano_infer_engine/paged_cache.py:300-322
+ *   last-token rows      nano_infer_engine/generation/paged_prefill.py:154
+ *
+ * plan is int32 [3, num_requests] (device): row 0 = block-table row, row 1 =
+ * context length (tokens already cached), row 2 = query length, one column
+ * per request in ragged order.  block_tables is an int32
+ * [num_rows, table_stride] array of physical block ids (logical order).
+ * Outputs (device, caller-allocated):
+ *   query_start_loc  int64 [R+1]   0, cumsum(query_length)
+ *   positions        int64 [T]     context_length + j for the j-th query token
+ *   slot_mapping     int64 [T]     table[pos / bs] * bs + pos % bs (-1 if bad)
+ *   seq_lens         int32 [R]     context_length + query_length
+ *   last_token_index int64 [R]     query_start_loc[r+1] - 1
+ *   token_request    int32 [T]     request index of each token
+ *   decode_list      int32 [R]     requests with query_length == 1, in order
+ *   prefill_list     int32 [R]     requests with query_length > 1, in order
+ *   list_counts      int32 [2]     {#decode, #prefill}
+ * T = num_tokens must equal sum(query_length).  Any output pointer except
+ * query_start_loc/positions/slot_mapping/seq_lens may be NULL.
+ */
+int nie_pack_ragged(const int32_t* plan, int32_t num_requests, int64_t num_tokens,
+                    const int32_t* block_tables, int64_t table_stride,
+                    int32_t block_size, int64_t num_blocks,
+                    int64_t* query_start_loc, int64_t* positions,
+                    int64_t* slot_mapping, int32_t* seq_lens,
+                    int64_t* last_token_index, int32_t* token_request,
+                    int32_t* decode_list, int32_t* prefill_list,
+                    int32_t* list_counts, int32_t* err_flag, void* stream);
+
+/*
+ * (b) Paged KV slot write.
+ * Replaces PagedKVCache.write (nano_infer_engine/paged_cache.py:324-382):
+ * key_cache[layer, slot / bs, slot % bs] = keys[t] (and values) for every t
+ * with slot_mapping[t] >= 0.  keys/values are contiguous [T, kv_heads,
+ * head_dim] of `dtype`; the copy is bit-exact.
+ */
+int nie_write_kv(const void* keys, const void* values, int64_t num_tokens,
+                 void* key_cache, void* value_cache, int32_t dtype, int32_t layer,
+                 int64_t num_layers, int64_t num_blocks, int32_t block_size,
+                 int32_t kv_heads, int32_t head_dim, const int64_t* slot_mapping,
+                 int32_t* err_flag, void* stream);
+
+/*
+ * Paged KV gather into contiguous [T, kv_heads, head_dim] tensors.
+ * Replaces PagedKVCache.gather (nano_infer_engine/paged_cache.py:384-422):
+ * out[t] = cache[layer, table[t / bs], t % bs] for t in [0, num_tokens).
+ * block_table is the sequence's int32 row (logical block order).
+ */
+int nie_gather_kv(const void* key_cache, const void* value_cache, int32_t dtype,
+                  int32_t layer, int64_t num_layers, int64_t num_blocks,
+                  int32_t block_size, int32_t kv_heads, int32_t head_dim,
+                  const int32_t* block_table, int64_t num_tokens, void* out_keys,
+                  void* out_values, int32_t* err_flag, void* stream);
+
+/*
+ * (e) Block copy between two paged pools (same or peer device).
+ * Replaces PagedKVCache.export_sequence / import_sequence
+ * (nano_infer_engine/paged_cache.py:205-298) and the per-block cross-device
+ * copy_ of the P/D handoff (nano_infer_engine/generation/pd_scheduler.py:
+ * 253-262).  For every layer l and logical block j < num_copy_blocks:
+ *   dst[l, dst_blocks[j]] = src[l, src_blocks[j]]
+ * and, when tail_valid_tokens in (0, block_size), token rows
+ * [tail_valid_tokens, block_size) of the LAST copied block are written as
+ * zeros (the zeroed export tail, paged_cache.py:225-229).  src_blocks or
+ * dst_blocks may be NULL meaning the identity (j), which lets a dense
+ * [L, n, bs, H, D] transfer tensor act as either side.  The kernel runs on
+ * the stream's device; a peer pointer (after nie_enable_peer_access) makes it
+ * a direct NVLink copy with 16-byte vector loads/stores.
+ */
+int nie_copy_blocks(const void* src_keys, const void* src_values,
+                    int64_t src_num_blocks, const int32_t* src_blocks,
+                    void* dst_keys, void* dst_values, int64_t dst_num_blocks,
+                    const int32_t* dst_blocks, int64_t num_copy_blocks,
+                    int32_t tail_valid_tokens, int32_t dtype, int64_t num_layers,
+                    int32_t block_size, int32_t kv_heads, int32_t head_dim,
+                    int32_t* err_flag, void* stream);
+
+/* Enable access from `device` to memory of `peer_device` (idempotent). */
+int nie_enable_peer_access(int device, int peer_device);
+
+/*
+ * (c) Paged decode attention: one query token per request.
+ * Replaces batched_paged_attention_reference
+ * (nano_infer_engine/layers/paged_attention.py:117-176, per-sequence body
+ * :4-114): for request r (= req_list[i] if req_list else i) with query row
+ * qr (= q_rows[r] if q_rows else r), block-table row tr (= table_rows[r] if
+ * table_rows else r) and n = seq_lens[r] cached tokens:
+ *   out[qr, h] = softmax(q[qr, h] . K[0:n, h / G]^T * scale) V[0:n, h / G]
+ * with G = q_heads / kv_heads.  q/out rows are [q_heads, head_dim]
+ * contiguous with row stride `q_row_stride` / `out_row_stride` elements.
+ * Numerics follow the reference: the dot product is rounded to `dtype`,
+ * multiplied by `scale`, rounded again, and the softmax runs in fp32.
+ *
+ * bf16 / head_dim 64 / block_size 16 uses the split-K TMA kernel, which needs
+ * `workspace` of nie_paged_decode_workspace_size() bytes (scratch; contents
+ * need no initialisation); other shapes use a generic kernel and ignore it.
+ */
+size_t nie_paged_decode_workspace_size(int device, int32_t num_requests,
+                                       int32_t q_heads, int32_t head_dim);
+
+int nie_paged_decode(const void* q, int64_t q_row_stride, void* out,
+                     int64_t out_row_stride, const void* key_cache,
+                     const void* value_cache, int32_t dtype, int32_t layer,
+                     int64_t num_layers, int64_t num_blocks, int32_t block_size,
+                     int32_t kv_heads, int32_t head_dim, int32_t q_heads,
+                     const int32_t* block_tables, int64_t table_stride,
+                     const int32_t* table_rows, const int32_t* seq_lens,
+                     const int64_t* q_rows, const int32_t* req_list,
+                     int32_t num_requests, float scale, void* workspace,
+                     size_t workspace_bytes, int32_t* err_flag, void* stream);
+
+/*
+ * (d) Varlen causal attention over the paged cache (chunked prefill, and the
+ * prefill rows of a mixed step).  Replaces the per-request write/gather/
+ * attention loop of GroupedQueryAttention.forward_ragged
+ * (nano_infer_engine/layers/attention.py:554-590) and the dense paged
+ * prefill (nano_infer_engine/models/llama.py:274-325 with
+ * attention.py:451-519).  The new keys/values must already be written into
+ * the cache (nie_write_kv).  For request r = req_list[i] (or i), its query
+ * tokens are rows [query_start_loc[r], query_start_loc[r+1]) of q/out; the
+ * token at offset j has position seq_lens[r] - qlen + j and attends to cached
+ * positions [0, position].
+ */
+int nie_varlen_attention(const void* q, void* out, int64_t row_stride,
+                         const void* key_cache, const void* value_cache,
+                         int32_t dtype, int32_t layer, int64_t num_layers,
+                         int64_t num_blocks, int32_t block_size, int32_t kv_heads,
+                         int32_t head_dim, int32_t q_heads,
+                         const int32_t* block_tables, int64_t table_stride,
+                         const int32_t* table_rows, const int32_t* seq_lens,
+                         const int64_t* query_start_loc, const int32_t* req_list,
+                         int32_t num_requests, int32_t max_query_len, float scale,
+                         int32_t* err_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NIE_B200_H */

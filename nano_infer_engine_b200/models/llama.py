@@ -1,0 +1,339 @@
+"""Llama-3.2 model with the reference's API, running attention on the sm_100a path.
+
+Reference: nano_infer_engine/models/llama.py.  ``LlamaConfig`` and the
+state-dict names are identical, so a checkpoint or random state dict loads
+into either engine.  All paged entry points (``forward`` with a
+``PagedKVCache`` and ``forward_ragged``) are executed as one *ragged step*:
+
+1. host: validation and block allocation (``ensure_capacity``) exactly as
+   the reference, in the same order, so block tables are bit-identical;
+2. device: kernel (a) expands the per-request plan into positions, slot
+   mapping, query_start_loc and decode/prefill lists;
+3. per layer: projections + RoPE (torch), slot write (b), decode (c) and
+   varlen (d) attention, o_proj and MLP (torch);
+4. host: ``advance`` per sequence.
+
+Logits are computed for every token, as the reference returns them, unless
+the caller (this package's ``paged_prefill``/``paged_prefill_chunks``) marks
+that only each request's last row is read; then only those rows go through
+the final norm and ``lm_head`` (reference llama.py:391 computes all rows
+and paged_prefill.py:154-155 keeps the last ones).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+from torch import nn
+
+from .. import ops
+from ..layers.decoder import Llama3Decoder
+from ..layers.rms_norm import RmsNorm
+from ..layers.rope import Rope, RopeScale
+from ..paged_cache import PagedKVCache
+
+# Attribute a caller sets on the input-id (or query_start_loc) tensor to ask
+# for last-row logits only; the returned logits carry LAST_ROWS_DONE = True
+# when the request was honoured.
+LAST_ROWS_ONLY = "_nie_last_rows_only"
+LAST_ROWS_DONE = "_nie_last_rows"
+HOST_BOUNDARIES = "_nie_host_boundaries"
+
+
+@dataclass
+class RopeScalingConfig:
+    factor: float = 32.0
+    low_freq_factor: float = 1.0
+    high_freq_factor: float = 4.0
+    original_max_position_embeddings: int = 8192
+
+
+@dataclass
+class LlamaConfig:
+    """Same fields and defaults as reference models/llama.py:22-70."""
+
+    vocab_size: int = 128256
+    hidden_size: int = 2048
+    mlp_inner_size: int = 8192
+    num_layers: int = 16
+    q_head_num: int = 32
+    kv_head_num: int = 8
+    norm_eps: float = 1e-5
+    rope_type: str = "llama3"
+    rope_theta: float = 500000.0
+    max_seq_len: int = 131072
+    rope_scaling: RopeScalingConfig = field(default_factory=RopeScalingConfig)
+    hidden_act: str = "silu"
+    attention_bias: bool = False
+    mlp_bias: bool = False
+    attention_dropout: float = 0.0
+    tie_word_embeddings: bool = True
+    initializer_range: float = 0.02
+    bos_token_id: int = 128000
+    eos_token_id: int = 128001
+
+    def __post_init__(self) -> None:
+        assert self.hidden_size % self.q_head_num == 0
+        assert self.q_head_num % self.kv_head_num == 0
+        assert self.head_dim % 2 == 0
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.q_head_num
+
+    @property
+    def group_num(self) -> int:
+        return self.q_head_num // self.kv_head_num
+
+
+def build_rope(config: LlamaConfig) -> Rope:
+    if config.rope_type == "default":
+        return Rope(dim=config.head_dim, theta_base=config.rope_theta)
+    if config.rope_type == "llama3":
+        s = config.rope_scaling
+        return RopeScale(
+            dim=config.head_dim,
+            theta_base=config.rope_theta,
+            scaling_factor=s.factor,
+            low_freq_factor=s.low_freq_factor,
+            high_freq_factor=s.high_freq_factor,
+            original_max_position_embeddings=s.original_max_position_embeddings,
+        )
+    raise ValueError(f"Unsupported rope type: {config.rope_type}")
+
+
+def init_random_weights_(model: nn.Module, seed: int, std: float = 0.02) -> nn.Module:
+    """Seeded N(0, std) weights, norms = 1, identical for any module with the same state-dict names.
+
+    Tensors are visited in sorted name order and drawn in fp32 on the CPU from
+    one ``torch.Generator``; tied tensors are filled once.  Works on this
+    package's model and on the reference's (same names), which is how both
+    engines get identical random-init weights.
+    """
+    gen = torch.Generator().manual_seed(seed)
+    state = model.state_dict()
+    seen: set[int] = set()
+    with torch.no_grad():
+        for name in sorted(state):
+            tensor = state[name]
+            if tensor.data_ptr() in seen:
+                continue
+            seen.add(tensor.data_ptr())
+            if name.endswith("norm.weight") or name.endswith("final_rms.weight"):
+                tensor.fill_(1.0)
+            else:
+                draw = torch.empty(tensor.shape, dtype=torch.float32).normal_(0.0, std, generator=gen)
+                tensor.copy_(draw.to(tensor.dtype))
+    return model
+
+
+class Llama3_2(nn.Module):
+    """Reference models/llama.py:95-394 module tree and entry points."""
+
+    def __init__(self, config: LlamaConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.embed = nn.Embedding(config.vocab_size, config.hidden_size)
+        self.rope = build_rope(config)
+        self.decoders = nn.ModuleList(
+            [
+                Llama3Decoder(
+                    config.norm_eps,
+                    config.q_head_num,
+                    config.kv_head_num,
+                    config.hidden_size,
+                    config.mlp_inner_size,
+                    self.rope,
+                )
+                for _ in range(config.num_layers)
+            ]
+        )
+        self.final_rms = RmsNorm(config.hidden_size, config.norm_eps)
+        self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
+        if config.tie_word_embeddings:
+            self.lm_head.weight = self.embed.weight
+
+    # ------------------------------------------------------------ core step
+    def run_ragged(
+        self,
+        input_ids: torch.Tensor,
+        meta: ops.RaggedMeta,
+        cache: PagedKVCache,
+        *,
+        rope_positions: torch.Tensor | None = None,
+        logit_rows: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        """Embed -> decoders -> norm -> lm_head over flattened tokens."""
+        x = self.embed(input_ids)
+        positions = meta.positions if rope_positions is None else rope_positions
+        sin, cos = self.rope.sin_cos(positions, x.dtype)
+        for layer_index, decoder in enumerate(self.decoders):
+            x = decoder.step(x, meta, cache, layer_index, sin, cos)
+        if logit_rows is not None:
+            x = x.index_select(0, logit_rows)
+        return self.lm_head(self.final_rms(x))
+
+    # -------------------------------------------------------- ragged entry
+    def forward_ragged(
+        self,
+        input_ids: torch.Tensor,
+        *,
+        kv_cache: PagedKVCache,
+        sequence_ids: tuple[str, ...],
+        query_start_loc: torch.Tensor,
+    ) -> torch.Tensor:
+        """Flattened variable-query step (reference llama.py:339-394)."""
+        if input_ids.ndim != 1 or input_ids.numel() == 0:
+            raise ValueError("input_ids must be a non-empty 1D tensor")
+        if not isinstance(kv_cache, PagedKVCache):
+            raise TypeError("kv_cache must be a PagedKVCache")
+        if not sequence_ids or len(set(sequence_ids)) != len(sequence_ids):
+            raise ValueError("sequence_ids must be non-empty and unique")
+        if query_start_loc.ndim != 1 or query_start_loc.numel() != len(sequence_ids) + 1:
+            raise ValueError("query_start_loc must have one boundary per sequence")
+        if query_start_loc.device != input_ids.device:
+            raise ValueError("query_start_loc must be on the input device")
+        boundaries = getattr(query_start_loc, HOST_BOUNDARIES, None)
+        if boundaries is None:
+            boundaries = query_start_loc.tolist()
+        if boundaries[0] != 0 or boundaries[-1] != input_ids.numel():
+            raise ValueError("query_start_loc must span all input tokens")
+        if any(end <= start for start, end in zip(boundaries, boundaries[1:])):
+            raise ValueError("each ragged query must contain at least one token")
+
+        context_lengths = tuple(kv_cache.get_sequence_length(s) for s in sequence_ids)
+        query_lengths = tuple(b - a for a, b in zip(boundaries, boundaries[1:]))
+        for s, c, q in zip(sequence_ids, context_lengths, query_lengths):
+            if c + q > self.config.max_seq_len:
+                raise ValueError(f"Sequence length {c + q} exceeds max_seq_len={self.config.max_seq_len}")
+            kv_cache.ensure_capacity(s, c + q)
+
+        meta = kv_cache.pack(tuple(sequence_ids), context_lengths, query_lengths)
+        last_only = bool(getattr(query_start_loc, LAST_ROWS_ONLY, False))
+        logits = self.run_ragged(
+            input_ids, meta, kv_cache, logit_rows=meta.last_token_index if last_only else None
+        )
+        for s, q in zip(sequence_ids, query_lengths):
+            kv_cache.advance(s, q)
+        if last_only:
+            setattr(logits, LAST_ROWS_DONE, True)
+        return logits
+
+    # ------------------------------------------------------- batched entry
+    def forward(
+        self,
+        x: torch.Tensor,
+        kv_cache: PagedKVCache | None = None,
+        attention_mask: torch.Tensor | None = None,
+        position_ids: torch.Tensor | None = None,
+        sequence_id: str = "default",
+        sequence_ids: tuple[str, ...] | None = None,
+    ) -> torch.Tensor:
+        """Batched paged decode / equal-length paged prefill (reference llama.py:127-337).
+
+        ``kv_cache=None`` runs a causal prefill through a temporary paged
+        cache (no padding masks).  The reference's contiguous ``KVCache`` and
+        left-padded dense paths are not part of this build.
+        """
+        if kv_cache is None:
+            return self._forward_uncached(x, attention_mask, position_ids)
+        if not isinstance(kv_cache, PagedKVCache):
+            raise NotImplementedError("only PagedKVCache is supported by nano_infer_engine_b200")
+        batch, seq_len = x.shape[0], x.shape[1]
+        decode = seq_len == 1
+        if sequence_ids is None:
+            if batch != 1:
+                raise ValueError("sequence_ids is required for batched paged inference")
+            ids: tuple[str, ...] = (sequence_id,)
+        else:
+            if not isinstance(sequence_ids, tuple):
+                raise TypeError("sequence_ids must be a tuple")
+            if len(sequence_ids) != batch:
+                raise ValueError("sequence_ids must match the batch size")
+            if any(not isinstance(s, str) or not s for s in sequence_ids):
+                raise ValueError("sequence IDs must be non-empty strings")
+            if len(set(sequence_ids)) != len(sequence_ids):
+                raise ValueError("sequence IDs must be unique within a batch")
+            ids = sequence_ids
+        lengths = tuple(kv_cache.get_sequence_length(s) for s in ids)
+        if not decode and len(set(lengths)) != 1:
+            raise ValueError("batched paged prefill currently requires equal sequence lengths")
+        kv_position = lengths[0]
+        total = max(lengths) + 1 if decode else kv_position + seq_len
+        if total > self.config.max_seq_len:
+            raise ValueError(f"Sequence length {total} exceeds max_seq_len={self.config.max_seq_len}")
+        for s, n in zip(ids, lengths):
+            kv_cache.ensure_capacity(s, n + 1 if decode else total)
+
+        if decode:
+            if attention_mask is not None:
+                if attention_mask.device != x.device:
+                    raise ValueError("attention_mask must be on the same device as x")
+                if not bool(attention_mask.all()):
+                    raise ValueError("paged inference does not support padding masks")
+            if position_ids is not None:
+                if position_ids.shape != (batch, 1):
+                    raise ValueError(
+                        f"position_ids must have shape {(batch, 1)}, got {tuple(position_ids.shape)}"
+                    )
+                if position_ids.device != x.device:
+                    raise ValueError("position_ids must be on the same device as x")
+                expected = torch.tensor(lengths, dtype=torch.long, device=x.device)[:, None]
+                if not torch.equal(position_ids, expected):
+                    raise ValueError("position_ids must match paged cache sequence lengths")
+            rope_positions = None
+        else:
+            if attention_mask is not None:
+                if attention_mask.shape != (batch, total):
+                    raise ValueError(
+                        f"attention_mask must have shape {(batch, total)}, got {tuple(attention_mask.shape)}"
+                    )
+                if attention_mask.device != x.device:
+                    raise ValueError("attention_mask must be on the same device as x")
+                if not bool(attention_mask.bool().all()):
+                    raise ValueError("paged inference does not support padding masks")
+            rope_positions = None
+            if position_ids is not None:
+                if position_ids.shape != (batch, seq_len):
+                    raise ValueError(
+                        f"position_ids must have shape {(batch, seq_len)}, got {tuple(position_ids.shape)}"
+                    )
+                if position_ids.device != x.device:
+                    raise ValueError("position_ids must be on the same device as x")
+                rope_positions = position_ids.reshape(-1)
+
+        meta = kv_cache.pack(ids, lengths, (seq_len,) * batch)
+        last_only = bool(getattr(x, LAST_ROWS_ONLY, False))
+        logits = self.run_ragged(
+            x.reshape(-1),
+            meta,
+            kv_cache,
+            rope_positions=rope_positions,
+            logit_rows=meta.last_token_index if last_only else None,
+        )
+        for s in ids:
+            kv_cache.advance(s, seq_len)
+        if last_only:
+            return logits.view(batch, 1, -1)
+        return logits.view(batch, seq_len, -1)
+
+    def _forward_uncached(self, x, attention_mask, position_ids) -> torch.Tensor:
+        if attention_mask is not None and not bool(attention_mask.bool().all()):
+            raise NotImplementedError("padding masks (left-padded dense batches) are not supported")
+        batch, seq_len = x.shape[0], x.shape[1]
+        if seq_len > self.config.max_seq_len:
+            raise ValueError(f"Sequence length {seq_len} exceeds max_seq_len={self.config.max_seq_len}")
+        block_size = 16
+        blocks = batch * (-(-seq_len // block_size))
+        cache = PagedKVCache(
+            blocks,
+            block_size,
+            self.config.num_layers,
+            self.config.kv_head_num,
+            self.config.head_dim,
+            self.embed.weight.dtype,
+            x.device,
+        )
+        ids = tuple(f"__uncached_{i}" for i in range(batch))
+        return self.forward(x, kv_cache=cache, position_ids=position_ids, sequence_ids=ids)

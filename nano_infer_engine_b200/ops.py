@@ -1,0 +1,466 @@
+"""Torch-facing wrappers of the C ABI: validate, then launch on the current stream.
+
+Every function here requires CUDA tensors and calls the sm_100a library; there
+is no CPU implementation.  Shapes follow the reference's cache layout
+``[num_layers, num_blocks, block_size, kv_heads, head_dim]``
+(nano_infer_engine/paged_cache.py:131-139).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ._native import (
+    NIE_DEV_ERR_BLOCK_RANGE,
+    NIE_DEV_ERR_CAPACITY,
+    NIE_DEV_ERR_SLOT_RANGE,
+    NIE_DEV_ERR_TIMEOUT,
+    NIE_DTYPE_BF16,
+    NIE_DTYPE_F16,
+    NIE_DTYPE_F32,
+    check,
+    lib,
+)
+
+_DTYPES = {
+    torch.float32: NIE_DTYPE_F32,
+    torch.bfloat16: NIE_DTYPE_BF16,
+    torch.float16: NIE_DTYPE_F16,
+}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype for the paged kernels: {dtype}") from None
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and t.device.type != "cuda":
+            raise RuntimeError(
+                "nano_infer_engine_b200 kernels require CUDA tensors "
+                f"(got a tensor on {t.device})"
+            )
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+# ------------------------------------------------------------ device errors
+_err_flags: dict[int, torch.Tensor] = {}
+
+
+def error_flag(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word the kernels OR their range/timeout bits into."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    flag = _err_flags.get(index)
+    if flag is None:
+        flag = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+        _err_flags[index] = flag
+    return flag
+
+
+_ERR_NAMES = {
+    NIE_DEV_ERR_BLOCK_RANGE: "block id outside the pool",
+    NIE_DEV_ERR_SLOT_RANGE: "slot outside the cache",
+    NIE_DEV_ERR_TIMEOUT: "bounded mbarrier wait timed out",
+    NIE_DEV_ERR_CAPACITY: "token position exceeds the block table",
+}
+
+
+def check_device_errors(device: torch.device, *, reset: bool = True) -> None:
+    """Synchronise on the flag and raise if any kernel reported a violation."""
+    flag = error_flag(device)
+    value = int(flag.item())
+    if value:
+        if reset:
+            flag.zero_()
+        names = [name for bit, name in _ERR_NAMES.items() if value & bit]
+        raise RuntimeError(f"device-side error flag {value:#x}: {', '.join(names)}")
+
+
+# ------------------------------------------------------------------ packing
+@dataclass
+class RaggedMeta:
+    """Device metadata of one ragged step, produced by :func:`pack_ragged`."""
+
+    query_start_loc: torch.Tensor  # int64 [R+1]
+    positions: torch.Tensor  # int64 [T]
+    slot_mapping: torch.Tensor  # int64 [T]
+    seq_lens: torch.Tensor  # int32 [R]
+    last_token_index: torch.Tensor  # int64 [R]
+    token_request: torch.Tensor  # int32 [T]
+    decode_list: torch.Tensor  # int32 [R]
+    prefill_list: torch.Tensor  # int32 [R]
+    list_counts: torch.Tensor  # int32 [2]
+    table_rows: torch.Tensor  # int32 [R]
+    block_tables: torch.Tensor  # int32 [rows, stride]
+    num_requests: int
+    num_tokens: int
+    num_decode: int
+    num_prefill: int
+    max_query_len: int
+
+
+def pack_ragged(
+    plan: torch.Tensor,
+    num_tokens: int,
+    block_tables: torch.Tensor,
+    block_size: int,
+    num_blocks: int,
+    *,
+    num_decode: int,
+    max_query_len: int,
+) -> RaggedMeta:
+    """Expand a per-request plan ``[3, R]`` (table rows, contexts, query lengths)."""
+    _require_cuda(plan, block_tables)
+    if plan.dtype != torch.int32 or plan.ndim != 2 or plan.shape[0] != 3 or not plan.is_contiguous():
+        raise ValueError("plan must be a contiguous int32 [3, R] tensor")
+    if block_tables.dtype != torch.int32 or block_tables.ndim != 2 or not block_tables.is_contiguous():
+        raise ValueError("block_tables must be a contiguous int32 [rows, stride] tensor")
+    device = plan.device
+    R = plan.shape[1]
+    T = int(num_tokens)
+    i64 = torch.empty(R + 1 + 3 * T + R, dtype=torch.int64, device=device)
+    i32 = torch.empty(4 * R + T + 2, dtype=torch.int32, device=device)
+    qsl = i64[: R + 1]
+    positions = i64[R + 1 : R + 1 + T]
+    slots = i64[R + 1 + T : R + 1 + 2 * T]
+    last = i64[R + 1 + 2 * T : R + 1 + 2 * T + R]
+    seq_lens = i32[:R]
+    dec = i32[R : 2 * R]
+    pf = i32[2 * R : 3 * R]
+    tok_req = i32[3 * R : 3 * R + T]
+    counts = i32[3 * R + T : 3 * R + T + 2]
+    status = lib.nie_pack_ragged(
+        plan.data_ptr(),
+        R,
+        T,
+        block_tables.data_ptr(),
+        block_tables.shape[1],
+        block_size,
+        num_blocks,
+        qsl.data_ptr(),
+        positions.data_ptr(),
+        slots.data_ptr(),
+        seq_lens.data_ptr(),
+        last.data_ptr(),
+        tok_req.data_ptr(),
+        dec.data_ptr(),
+        pf.data_ptr(),
+        counts.data_ptr(),
+        error_flag(device).data_ptr(),
+        _stream(device),
+    )
+    check(status, "nie_pack_ragged")
+    return RaggedMeta(
+        query_start_loc=qsl,
+        positions=positions,
+        slot_mapping=slots,
+        seq_lens=seq_lens,
+        last_token_index=last,
+        token_request=tok_req,
+        decode_list=dec,
+        prefill_list=pf,
+        list_counts=counts,
+        table_rows=plan[0],
+        block_tables=block_tables,
+        num_requests=R,
+        num_tokens=T,
+        num_decode=int(num_decode),
+        num_prefill=R - int(num_decode),
+        max_query_len=int(max_query_len),
+    )
+
+
+# --------------------------------------------------------------- KV moves
+def _cache_geometry(key_cache: torch.Tensor) -> tuple[int, int, int, int, int]:
+    if key_cache.ndim != 5 or not key_cache.is_contiguous():
+        raise ValueError("caches must be contiguous 5D tensors")
+    L, nb, bs, h, d = key_cache.shape
+    return L, nb, bs, h, d
+
+
+def write_kv(
+    keys: torch.Tensor,
+    values: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    slot_mapping: torch.Tensor,
+) -> None:
+    """Scatter ``keys/values [T, H, D]`` into the cache slots (bit-exact copy)."""
+    _require_cuda(keys, values, key_cache, value_cache, slot_mapping)
+    L, nb, bs, h, d = _cache_geometry(key_cache)
+    if keys.shape != values.shape or keys.ndim != 3 or keys.shape[1:] != (h, d):
+        raise ValueError("keys/values must be [T, kv_heads, head_dim] matching the cache")
+    if keys.dtype != key_cache.dtype or values.dtype != value_cache.dtype:
+        raise ValueError("keys/values must match the cache dtype")
+    keys = keys.contiguous()
+    values = values.contiguous()
+    if slot_mapping.dtype != torch.int64 or slot_mapping.numel() < keys.shape[0]:
+        raise ValueError("slot_mapping must be int64 with one slot per token")
+    device = key_cache.device
+    status = lib.nie_write_kv(
+        keys.data_ptr(),
+        values.data_ptr(),
+        keys.shape[0],
+        key_cache.data_ptr(),
+        value_cache.data_ptr(),
+        dtype_code(key_cache.dtype),
+        layer,
+        L,
+        nb,
+        bs,
+        h,
+        d,
+        slot_mapping.data_ptr(),
+        error_flag(device).data_ptr(),
+        _stream(device),
+    )
+    check(status, "nie_write_kv")
+
+
+def gather_kv(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_table: torch.Tensor,
+    num_tokens: int,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gather a sequence's first ``num_tokens`` K/V rows into contiguous tensors."""
+    _require_cuda(key_cache, value_cache, block_table)
+    L, nb, bs, h, d = _cache_geometry(key_cache)
+    if block_table.dtype != torch.int32 or not block_table.is_contiguous():
+        raise ValueError("block_table must be a contiguous int32 tensor")
+    out_k = torch.empty((num_tokens, h, d), dtype=key_cache.dtype, device=key_cache.device)
+    out_v = torch.empty_like(out_k)
+    device = key_cache.device
+    status = lib.nie_gather_kv(
+        key_cache.data_ptr(),
+        value_cache.data_ptr(),
+        dtype_code(key_cache.dtype),
+        layer,
+        L,
+        nb,
+        bs,
+        h,
+        d,
+        block_table.data_ptr(),
+        num_tokens,
+        out_k.data_ptr(),
+        out_v.data_ptr(),
+        error_flag(device).data_ptr(),
+        _stream(device),
+    )
+    check(status, "nie_gather_kv")
+    return out_k, out_v
+
+
+def copy_blocks(
+    src_keys: torch.Tensor,
+    src_values: torch.Tensor,
+    src_blocks: torch.Tensor | None,
+    dst_keys: torch.Tensor,
+    dst_values: torch.Tensor,
+    dst_blocks: torch.Tensor | None,
+    num_copy_blocks: int,
+    tail_valid_tokens: int,
+    *,
+    run_on: torch.device | None = None,
+) -> None:
+    """Copy logical blocks between two paged pools (see ``nie_copy_blocks``).
+
+    ``run_on`` selects the device whose stream runs the kernel (default: the
+    destination).  Source and destination may live on different GPUs; peer
+    access is enabled on demand.
+    """
+    _require_cuda(src_keys, src_values, dst_keys, dst_values, src_blocks, dst_blocks)
+    L, snb, bs, h, d = _cache_geometry(src_keys)
+    L2, dnb, bs2, h2, d2 = _cache_geometry(dst_keys)
+    if (L, bs, h, d) != (L2, bs2, h2, d2) or src_keys.dtype != dst_keys.dtype:
+        raise ValueError("source and destination pools must share layout and dtype")
+    run_device = run_on if run_on is not None else dst_keys.device
+    for other in (src_keys.device, dst_keys.device):
+        if other != run_device:
+            enable_peer_access(run_device, other)
+    with torch.cuda.device(run_device):
+        status = lib.nie_copy_blocks(
+            src_keys.data_ptr(),
+            src_values.data_ptr(),
+            snb,
+            _ptr(src_blocks),
+            dst_keys.data_ptr(),
+            dst_values.data_ptr(),
+            dnb,
+            _ptr(dst_blocks),
+            int(num_copy_blocks),
+            int(tail_valid_tokens),
+            dtype_code(src_keys.dtype),
+            L,
+            bs,
+            h,
+            d,
+            error_flag(run_device).data_ptr(),
+            _stream(run_device),
+        )
+    check(status, "nie_copy_blocks")
+
+
+_peer_enabled: set[tuple[int, int]] = set()
+
+
+def enable_peer_access(device: torch.device, peer: torch.device) -> None:
+    key = (device.index, peer.index)
+    if key in _peer_enabled:
+        return
+    check(lib.nie_enable_peer_access(device.index, peer.index), "nie_enable_peer_access")
+    _peer_enabled.add(key)
+
+
+# --------------------------------------------------------------- attention
+_workspaces: dict[int, torch.Tensor] = {}
+
+
+def decode_workspace(device: torch.device, num_requests: int, q_heads: int, head_dim: int) -> torch.Tensor:
+    """Reusable split-K scratch for :func:`paged_decode` on ``device``."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    need = int(lib.nie_paged_decode_workspace_size(index, num_requests, q_heads, head_dim))
+    ws = _workspaces.get(index)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", index))
+        _workspaces[index] = ws
+    return ws
+
+
+def paged_decode(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    *,
+    out: torch.Tensor | None = None,
+    table_rows: torch.Tensor | None = None,
+    q_rows: torch.Tensor | None = None,
+    req_list: torch.Tensor | None = None,
+    num_requests: int | None = None,
+    scale: float | None = None,
+) -> torch.Tensor:
+    """Single-token paged attention for ``query [rows, q_heads, head_dim]``."""
+    _require_cuda(query, key_cache, value_cache, block_tables, seq_lens, table_rows, q_rows, req_list)
+    L, nb, bs, h, d = _cache_geometry(key_cache)
+    if query.ndim != 3 or query.shape[2] != d or query.stride(2) != 1 or query.stride(1) != d:
+        raise ValueError("query must be [rows, q_heads, head_dim] with contiguous rows")
+    if query.dtype != key_cache.dtype:
+        raise ValueError("query and caches must share a dtype")
+    if block_tables.dtype != torch.int32 or block_tables.ndim != 2 or block_tables.stride(1) != 1:
+        raise ValueError("block_tables must be int32 [rows, stride] with contiguous rows")
+    if seq_lens.dtype != torch.int32:
+        raise ValueError("seq_lens must be int32")
+    R = int(num_requests if num_requests is not None else seq_lens.numel())
+    hq = query.shape[1]
+    if out is None:
+        out = torch.empty_like(query)
+    device = query.device
+    ws = decode_workspace(device, max(R, 1), hq, d)
+    status = lib.nie_paged_decode(
+        query.data_ptr(),
+        query.stride(0),
+        out.data_ptr(),
+        out.stride(0),
+        key_cache.data_ptr(),
+        value_cache.data_ptr(),
+        dtype_code(query.dtype),
+        layer,
+        L,
+        nb,
+        bs,
+        h,
+        d,
+        hq,
+        block_tables.data_ptr(),
+        block_tables.stride(0),
+        _ptr(table_rows),
+        seq_lens.data_ptr(),
+        _ptr(q_rows),
+        _ptr(req_list),
+        R,
+        float(d**-0.5 if scale is None else scale),
+        ws.data_ptr(),
+        ws.numel(),
+        error_flag(device).data_ptr(),
+        _stream(device),
+    )
+    check(status, "nie_paged_decode")
+    return out
+
+
+def varlen_attention(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    query_start_loc: torch.Tensor,
+    max_query_len: int,
+    *,
+    out: torch.Tensor | None = None,
+    table_rows: torch.Tensor | None = None,
+    req_list: torch.Tensor | None = None,
+    num_requests: int | None = None,
+    scale: float | None = None,
+) -> torch.Tensor:
+    """Causal varlen attention of ragged query rows over the paged cache."""
+    _require_cuda(query, key_cache, value_cache, block_tables, seq_lens, query_start_loc, table_rows, req_list)
+    L, nb, bs, h, d = _cache_geometry(key_cache)
+    if query.ndim != 3 or query.shape[2] != d or query.stride(2) != 1 or query.stride(1) != d:
+        raise ValueError("query must be [rows, q_heads, head_dim] with contiguous rows")
+    if query_start_loc.dtype != torch.int64:
+        raise ValueError("query_start_loc must be int64")
+    R = int(num_requests if num_requests is not None else seq_lens.numel())
+    hq = query.shape[1]
+    if out is None:
+        out = torch.empty_like(query)
+    if out.stride(0) != query.stride(0):
+        raise ValueError("out must share the query row stride")
+    device = query.device
+    status = lib.nie_varlen_attention(
+        query.data_ptr(),
+        out.data_ptr(),
+        query.stride(0),
+        key_cache.data_ptr(),
+        value_cache.data_ptr(),
+        dtype_code(query.dtype),
+        layer,
+        L,
+        nb,
+        bs,
+        h,
+        d,
+        hq,
+        block_tables.data_ptr(),
+        block_tables.stride(0),
+        _ptr(table_rows),
+        seq_lens.data_ptr(),
+        query_start_loc.data_ptr(),
+        _ptr(req_list),
+        R,
+        int(max_query_len),
+        float(d**-0.5 if scale is None else scale),
+        error_flag(device).data_ptr(),
+        _stream(device),
+    )
+    check(status, "nie_varlen_attention")
+    return out

@@ -1,0 +1,251 @@
+"""Kernel parity on the GPU: every C-ABI kernel against the CPU oracle / reference goldens.
+
+Integer and byte work (packing, slot write, gather, block copy) must be
+bit-exact; attention must be within max-abs 2e-2 (bf16) / 1e-4 (fp32) of the
+oracle.
+"""
+
+from pathlib import Path
+
+import pytest
+import torch
+
+import recipes
+from oracle import attention as oatt
+from oracle.paging import OracleTables, ragged_metadata
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TOL = {torch.bfloat16: 2e-2, torch.float32: 1e-4}
+
+
+def ops():
+    from nano_infer_engine_b200 import ops as _ops
+
+    return _ops
+
+
+def _tables_tensor(tables, device, width=None):
+    width = width or max(len(t) for t in tables)
+    out = torch.full((len(tables), width), -1, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        out[i, : len(t)] = torch.tensor(t, dtype=torch.int32)
+    return out.to(device)
+
+
+def _random_layout(num_blocks, seq_lens, bs, seed):
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(num_blocks, generator=g).tolist()
+    tables, at = [], 0
+    for n in seq_lens:
+        nb = (n + bs - 1) // bs
+        tables.append(perm[at : at + nb])
+        at += nb
+    return tables
+
+
+# ------------------------------------------------------------------ (a)
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_pack_ragged_bit_exact(cuda, seed):
+    g = torch.Generator().manual_seed(seed)
+    bs, nb = 16, 4096
+    R = int(torch.randint(1, 300, (1,), generator=g))
+    contexts = torch.randint(0, 3000, (R,), generator=g).tolist()
+    qlens = [1 if torch.rand(1, generator=g).item() < 0.6 else int(torch.randint(2, 200, (1,), generator=g)) for _ in range(R)]
+    tables = _random_layout(nb * 8, [c + q for c, q in zip(contexts, qlens)], bs, seed)
+    tables = [[b % nb for b in t] for t in tables]
+    rows = torch.randperm(R, generator=g).tolist()  # requests live in arbitrary table rows
+    table_dev = torch.full((R, max(len(t) for t in tables) + 3), -1, dtype=torch.int32)
+    for r, t in zip(rows, tables):
+        table_dev[r, : len(t)] = torch.tensor(t, dtype=torch.int32)
+    plan = torch.tensor([rows, contexts, qlens], dtype=torch.int32).to(cuda)
+    meta = ops().pack_ragged(plan, sum(qlens), table_dev.to(cuda), bs, nb,
+                             num_decode=sum(q == 1 for q in qlens), max_query_len=max(qlens))
+    want = ragged_metadata(tables, contexts, qlens, bs)
+    assert meta.query_start_loc.cpu().tolist() == want["query_start_loc"]
+    assert meta.positions.cpu().tolist() == want["positions"]
+    assert meta.slot_mapping.cpu().tolist() == want["slot_mapping"]
+    assert meta.seq_lens.cpu().tolist() == want["seq_lens"]
+    assert meta.last_token_index.cpu().tolist() == want["last_token_index"]
+    counts = meta.list_counts.cpu().tolist()
+    assert meta.decode_list[: counts[0]].cpu().tolist() == want["decode_list"]
+    assert meta.prefill_list[: counts[1]].cpu().tolist() == want["prefill_list"]
+    tok_req = meta.token_request.cpu().tolist()
+    assert tok_req == [r for r, q in enumerate(qlens) for _ in range(q)]
+    ops().check_device_errors(cuda)
+
+
+def test_pack_flags_unallocated_positions(cuda):
+    table = torch.tensor([[3, -1]], dtype=torch.int32, device=cuda)
+    plan = torch.tensor([[0], [10], [10]], dtype=torch.int32, device=cuda)  # positions 10..19, block 1 missing
+    meta = ops().pack_ragged(plan, 10, table, 16, 8, num_decode=0, max_query_len=10)
+    slots = meta.slot_mapping.cpu().tolist()
+    assert slots[:6] == [3 * 16 + p for p in range(10, 16)]
+    assert slots[6:] == [-1] * 4
+    with pytest.raises(RuntimeError, match="block id outside the pool"):
+        ops().check_device_errors(cuda)
+
+
+# ------------------------------------------------------------------ (b)
+@pytest.mark.parametrize("dtype,hkv,hd", [(torch.bfloat16, 8, 64), (torch.float32, 2, 64), (torch.bfloat16, 2, 3)])
+def test_write_kv_bit_exact(cuda, dtype, hkv, hd):
+    g = torch.Generator().manual_seed(5)
+    L, nb, bs, T = 3, 64, 16, 200
+    kc = torch.randn(L, nb, bs, hkv, hd, generator=g).to(dtype)
+    vc = torch.randn(L, nb, bs, hkv, hd, generator=g).to(dtype)
+    k = torch.randn(T, hkv, hd, generator=g).to(dtype)
+    v = torch.randn(T, hkv, hd, generator=g).to(dtype)
+    slots = torch.randperm(nb * bs, generator=g)[:T]
+    slots[7] = -1  # skipped, like a slot the packer could not resolve
+    want_k, want_v = kc.clone(), vc.clone()
+    for t, s in enumerate(slots.tolist()):
+        if s >= 0:
+            want_k[1, s // bs, s % bs] = k[t]
+            want_v[1, s // bs, s % bs] = v[t]
+    dk, dv = kc.to(cuda), vc.to(cuda)
+    ops().write_kv(k.to(cuda), v.to(cuda), dk, dv, 1, slots.to(cuda))
+    assert torch.equal(dk.cpu(), want_k) and torch.equal(dv.cpu(), want_v)
+    ops().check_device_errors(cuda)
+
+
+def test_gather_kv_bit_exact(cuda):
+    g = torch.Generator().manual_seed(6)
+    kc = torch.randn(2, 40, 16, 8, 64, generator=g).to(torch.bfloat16)
+    vc = torch.randn(2, 40, 16, 8, 64, generator=g).to(torch.bfloat16)
+    table = [7, 3, 30, 11]
+    n = 53
+    gk, gv = ops().gather_kv(kc.to(cuda), vc.to(cuda), 1, torch.tensor(table, dtype=torch.int32, device=cuda), n)
+    assert torch.equal(gk.cpu(), oatt.gather_sequence(kc, 1, table, n))
+    assert torch.equal(gv.cpu(), oatt.gather_sequence(vc, 1, table, n))
+
+
+# ------------------------------------------------------------------ (e)
+@pytest.mark.parametrize("length", [16, 37, 1])
+def test_copy_blocks_export_semantics(cuda, length):
+    """Block copy with a zeroed tail == reference export_sequence (paged_cache.py:205-240)."""
+    g = torch.Generator().manual_seed(length)
+    L, nb, bs = 3, 20, 16
+    kc = torch.randn(L, nb, bs, 8, 64, generator=g).to(torch.bfloat16)
+    vc = torch.randn(L, nb, bs, 8, 64, generator=g).to(torch.bfloat16)
+    n = (length + bs - 1) // bs
+    src = torch.randperm(nb, generator=g)[:n].tolist()
+    dst_pool_k = torch.full((L, nb, bs, 8, 64), 7.0, dtype=torch.bfloat16)
+    dst_pool_v = dst_pool_k.clone()
+    dst = torch.randperm(nb, generator=g)[:n].tolist()
+    dk, dv = dst_pool_k.to(cuda), dst_pool_v.to(cuda)
+    ops().copy_blocks(kc.to(cuda), vc.to(cuda), torch.tensor(src, dtype=torch.int32, device=cuda), dk, dv,
+                      torch.tensor(dst, dtype=torch.int32, device=cuda), n, length % bs)
+    want_k, want_v = dst_pool_k.clone(), dst_pool_v.clone()
+    for j, (s, d) in enumerate(zip(src, dst)):
+        want_k[:, d] = kc[:, s]
+        want_v[:, d] = vc[:, s]
+    tail = length % bs
+    if tail:
+        want_k[:, dst[-1], tail:] = 0
+        want_v[:, dst[-1], tail:] = 0
+    assert torch.equal(dk.cpu(), want_k) and torch.equal(dv.cpu(), want_v)
+
+
+# ------------------------------------------------------------------ (c)
+@pytest.mark.parametrize("name", recipes.DECODE_CASES)
+def test_decode_matches_reference_golden(cuda, name):
+    case = recipes.decode_case(name)
+    golden = torch.load(GOLDEN / f"decode_{name}.pt")["out"]
+    tables = _tables_tensor(case["tables"], cuda)
+    lens = torch.tensor(case["seq_lens"], dtype=torch.int32, device=cuda)
+    out = ops().paged_decode(case["query"].to(cuda), case["key_cache"].to(cuda), case["value_cache"].to(cuda),
+                             case["layer"], tables, lens)
+    ops().check_device_errors(cuda)
+    tol = TOL[golden.dtype]
+    torch.testing.assert_close(out.cpu().float(), golden.float(), atol=tol, rtol=0)
+
+
+@pytest.mark.parametrize("seed,B,max_ctx", [(0, 64, 3000), (1, 7, 20000), (2, 130, 600), (3, 1, 29600)])
+def test_fast_decode_against_oracle(cuda, seed, B, max_ctx):
+    """bf16 / hd 64 / bs 16 split-K kernel, ragged lengths incl. 1 and block-aligned."""
+    g = torch.Generator().manual_seed(seed)
+    bs = 16
+    lens = torch.randint(1, max_ctx + 1, (B,), generator=g).tolist()
+    lens[0] = 1
+    if B > 2:
+        lens[1] = 16 * 7
+    total_blocks = sum((n + bs - 1) // bs for n in lens)
+    nb = total_blocks + 37
+    tables = _random_layout(nb, lens, bs, seed)
+    kc = torch.randn(1, nb, bs, 8, 64, generator=g).to(torch.bfloat16)
+    vc = torch.randn(1, nb, bs, 8, 64, generator=g).to(torch.bfloat16)
+    q = torch.randn(B, 32, 64, generator=g).to(torch.bfloat16)
+    dk, dv = kc.to(cuda), vc.to(cuda)
+    # poison the unused tail rows: masked positions must not leak (NaN * 0)
+    for t, n in zip(tables, lens):
+        if n % bs:
+            dk[0, t[-1], n % bs :] = float("nan")
+            dv[0, t[-1], n % bs :] = float("nan")
+    out = ops().paged_decode(q.to(cuda), dk, dv, 0, _tables_tensor(tables, cuda),
+                             torch.tensor(lens, dtype=torch.int32, device=cuda))
+    ops().check_device_errors(cuda)
+    want = oatt.paged_decode(q, kc, vc, tables, lens, 0)
+    assert torch.isfinite(out).all()
+    torch.testing.assert_close(out.cpu().float(), want.float(), atol=2e-2, rtol=0)
+
+
+def test_decode_with_indirection(cuda):
+    """req_list / table_rows / q_rows indirection as used for the decode rows of a mixed step."""
+    g = torch.Generator().manual_seed(9)
+    lens = [50, 1, 333, 17]
+    tables = _random_layout(80, lens, 16, 9)
+    kc = torch.randn(1, 80, 16, 8, 64, generator=g).to(torch.bfloat16)
+    vc = torch.randn(1, 80, 16, 8, 64, generator=g).to(torch.bfloat16)
+    q = torch.randn(10, 32, 64, generator=g).to(torch.bfloat16)
+    # requests 0..3 live in table rows 2,0,3,1; their query rows are 9,4,0,6; decode only 1 and 2
+    rows = [2, 0, 3, 1]
+    qrows = [9, 4, 0, 6]
+    t = [None] * 4
+    for r, row in enumerate(rows):
+        t[row] = tables[r]
+    out = torch.zeros(10, 32, 64, dtype=torch.bfloat16, device=cuda)
+    ops().paged_decode(q.to(cuda), kc.to(cuda), vc.to(cuda), 0, _tables_tensor(t, cuda),
+                       torch.tensor(lens, dtype=torch.int32, device=cuda), out=out,
+                       table_rows=torch.tensor(rows, dtype=torch.int32, device=cuda),
+                       q_rows=torch.tensor(qrows, dtype=torch.int64, device=cuda),
+                       req_list=torch.tensor([1, 2], dtype=torch.int32, device=cuda), num_requests=2)
+    want = oatt.paged_decode(q[[4, 0]], kc, vc, [tables[1], tables[2]], [lens[1], lens[2]], 0)
+    got = out.cpu()
+    torch.testing.assert_close(got[[4, 0]].float(), want.float(), atol=2e-2, rtol=0)
+    untouched = [i for i in range(10) if i not in (4, 0)]
+    assert torch.count_nonzero(got[untouched]) == 0
+
+
+def test_decode_bad_block_id_sets_flag_without_fault(cuda):
+    kc = torch.zeros(1, 8, 16, 8, 64, dtype=torch.bfloat16, device=cuda)
+    q = torch.zeros(1, 32, 64, dtype=torch.bfloat16, device=cuda)
+    table = torch.tensor([[1, 99]], dtype=torch.int32, device=cuda)
+    ops().paged_decode(q, kc, kc, 0, table, torch.tensor([20], dtype=torch.int32, device=cuda))
+    with pytest.raises(RuntimeError, match="block id outside the pool"):
+        ops().check_device_errors(cuda)
+    torch.cuda.synchronize()
+
+
+# ------------------------------------------------------------------ (d)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_varlen_against_oracle(cuda, dtype):
+    g = torch.Generator().manual_seed(21)
+    contexts = [0, 7, 300, 1000, 16, 5]
+    qlens = [5, 16, 129, 64, 1, 2]
+    bs, hkv, hq = 16, 8, 32
+    lens = [c + q for c, q in zip(contexts, qlens)]
+    nb = sum((n + bs - 1) // bs for n in lens) + 11
+    tables = _random_layout(nb, lens, bs, 21)
+    kc = torch.randn(2, nb, bs, hkv, 64, generator=g).to(dtype)
+    vc = torch.randn(2, nb, bs, hkv, 64, generator=g).to(dtype)
+    q = torch.randn(sum(qlens), hq, 64, generator=g).to(dtype)
+    qsl = [0]
+    for n in qlens:
+        qsl.append(qsl[-1] + n)
+    out = ops().varlen_attention(q.to(cuda), kc.to(cuda), vc.to(cuda), 1, _tables_tensor(tables, cuda),
+                                 torch.tensor(lens, dtype=torch.int32, device=cuda),
+                                 torch.tensor(qsl, dtype=torch.int64, device=cuda), max(qlens))
+    ops().check_device_errors(cuda)
+    want = oatt.varlen_attention(q, kc, vc, tables, contexts, qlens, 1)
+    torch.testing.assert_close(out.cpu().float(), want.float(), atol=TOL[dtype], rtol=0)
