@@ -1,0 +1,483 @@
+"""Benchmark of the B200 ragged-batch attention engine (one JSON line on rank 0).
+
+Headline: output tokens/s of continuous batching at
+Llama-3.2-1B shape on random-init bf16 weights (std 0.02): 16 requests,
+prompts U[128, 2048], 256 greedy new tokens each, prefill chunk 128, at most
+512 prefill tokens per step, block size 16, max model length 29600.  One
+"step" = one full generation of that batch through the public scheduler API.
+
+* ``value``   - tokens/s with prompts resident in HBM;
+* ``e2e``     - the same through the public API from pinned HOST prompts,
+                H2D of the prompts and D2H of every generated sequence inside
+                the timed region;
+* ``roofline``- the paged decode kernel on BASELINE config 3 (B=64, ctx
+                U[512, 29600], 131072-block pool), algorithmic bytes / CUDA-
+                event time vs the measured HBM copy bandwidth;
+* ``cpu_baseline`` - the CPU oracle (restated reference forward) on a bounded
+                sample of the same workload, extrapolated to tokens/s.
+
+N GPUs (torchrun): independent replicas, weak scaling, max-over-ranks time.
+``--impl reference`` times the reference algorithm on the host cores (the
+oracle port; rank 0 only) for the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "output tok/s at Llama-3.2-1B shape"
+UNIT = "tok/s"
+SEED = 1234
+
+
+# ------------------------------------------------------------------ helpers
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--requests", type=int, default=16)
+    p.add_argument("--new-tokens", type=int, default=256)
+    p.add_argument("--decode-iters", type=int, default=20)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--only", choices=("all", "engine", "decode"), default="all",
+                   help="engine: headline run only; decode: config-3 decode micro-bench only (profiling)")
+    p.add_argument("--decode-batch", type=int, default=64)
+    p.add_argument("--decode-blocks", type=int, default=131072)
+    return p.parse_args()
+
+
+def llama_1b_config(max_seq_len=29600):
+    from nano_infer_engine_b200.models.llama import LlamaConfig
+
+    return LlamaConfig(max_seq_len=max_seq_len)
+
+
+def workload(num_requests, seed=SEED):
+    g = torch.Generator().manual_seed(seed)
+    lengths = torch.randint(128, 2049, (num_requests,), generator=g).tolist()
+    return [torch.randint(0, 128256, (1, n), generator=g) for n in lengths]
+
+
+class ClockSampler:
+    """NVML clocks / throttle reasons sampled every 100 ms while running."""
+
+    REASONS = {
+        0x1: "gpu_idle",
+        0x2: "applications_clocks_setting",
+        0x4: "sw_power_cap",
+        0x8: "hw_slowdown",
+        0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, index):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM))
+                get = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or getattr(
+                    n, "nvmlDeviceGetCurrentClocksThrottleReasons")
+                self.reasons |= get(self.handle) & ~0x1
+            except Exception:
+                pass
+            time.sleep(0.1)
+
+    def __enter__(self):
+        if self.nvml:
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self.nvml:
+            self.thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        busy = [s for s in self.samples if s > 500] or self.samples
+        return {
+            "sm_mhz": statistics.median(busy),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": [name for bit, name in self.REASONS.items() if self.reasons & bit],
+        }
+
+
+# ---------------------------------------------------------- engine run
+def build_engine(device):
+    from nano_infer_engine_b200.models.llama import build_random_llama
+
+    return build_random_llama(llama_1b_config(), SEED, 0.02, torch.bfloat16, device)
+
+
+def make_cache(device, num_requests, max_tokens):
+    from nano_infer_engine_b200.paged_cache import PagedKVCache
+
+    blocks = num_requests * (-(-max_tokens // 16)) + 64
+    return PagedKVCache(blocks, 16, 16, 8, 64, torch.bfloat16, device)
+
+
+def generate(model, cache, prompts, new_tokens):
+    """One step: the whole batch through the public scheduler API."""
+    from nano_infer_engine_b200.generation.config import GenerationConfig
+    from nano_infer_engine_b200.generation.scheduler import ContinuousBatchingScheduler
+
+    config = GenerationConfig(max_new_tokens=new_tokens, prefill_chunk_size=128, max_prefill_tokens_per_step=512)
+    sched = ContinuousBatchingScheduler(model, config, cache, len(prompts))
+    reqs = [sched.add_request(f"req-{i}", p) for i, p in enumerate(prompts)]
+    sched.run_until_idle()
+    return reqs
+
+
+def time_engine(model, cache, prompts, new_tokens, steps, warmup, dist_ctx):
+    from nano_infer_engine_b200 import ops
+
+    for _ in range(warmup):
+        generate(model, cache, prompts, new_tokens)
+    torch.cuda.synchronize()
+    barrier(dist_ctx)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = ops.LAUNCHES
+    start.record()
+    for _ in range(steps):
+        generate(model, cache, prompts, new_tokens)
+    stop.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(stop) / 1e3, ops.LAUNCHES - launches0
+
+
+def time_e2e(model, cache, host_prompts, new_tokens, steps, device):
+    """Prompts start in pinned host memory; results are read back to the host."""
+    h2d = sum(p.numel() * p.element_size() for p in host_prompts)
+    d2h = 0
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        prompts = [p.to(device, non_blocking=True) for p in host_prompts]
+        reqs = generate(model, cache, prompts, new_tokens)
+        outs = [r.sequence.to("cpu") for r in reqs]
+        d2h = sum(o.numel() * o.element_size() for o in outs)
+    stop.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(stop) / 1e3, h2d, d2h
+
+
+# ------------------------------------------------------ decode roofline
+def decode_config3(device, iters, B=64, nb=131072):
+    """B=64, ctx U[512, 29600], pool 131072 blocks, 1 layer."""
+    from nano_infer_engine_b200 import ops
+
+    g = torch.Generator().manual_seed(0)
+    bs = 16
+    lens = torch.randint(512, 29601, (B,), generator=g).tolist()
+    if sum(-(-n // bs) for n in lens) > nb:
+        raise ValueError(f"decode pool of {nb} blocks cannot hold batch {B}")
+    perm = torch.randperm(nb, generator=g)
+    width = max(-(-n // bs) for n in lens)
+    tables = torch.full((B, width), -1, dtype=torch.int32)
+    at = 0
+    for i, n in enumerate(lens):
+        k = -(-n // bs)
+        tables[i, :k] = perm[at : at + k].to(torch.int32)
+        at += k
+    gen = torch.Generator(device=device).manual_seed(0)
+    kc = torch.randn((1, nb, bs, 8, 64), generator=gen, device=device, dtype=torch.bfloat16)
+    vc = torch.randn((1, nb, bs, 8, 64), generator=gen, device=device, dtype=torch.bfloat16)
+    q = torch.randn((B, 32, 64), generator=gen, device=device, dtype=torch.bfloat16)
+    tables_d = tables.to(device)
+    lens_d = torch.tensor(lens, dtype=torch.int32, device=device)
+    out = torch.empty_like(q)
+    for _ in range(3):
+        ops.paged_decode(q, kc, vc, 0, tables_d, lens_d, out=out)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        ops.paged_decode(q, kc, vc, 0, tables_d, lens_d, out=out)
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / iters
+    ops.check_device_errors(device)
+    sum_ctx = sum(lens)
+    algo_bytes = sum_ctx * 2048 + sum(-(-n // bs) for n in lens) * 4 + 2 * B * 32 * 64 * 2
+    del kc, vc
+    torch.cuda.empty_cache()
+    return {"ms": ms, "bytes": algo_bytes, "sum_ctx": sum_ctx, "batch": B}
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    path = ROOT / "profiles" / "decode_traffic.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_sample(prompts, model_cpu_state, threads):
+    """Reference algorithm (oracle port) on the host: one 512-token prefill step and
+    one 16-token decode step at the workload's context lengths; extrapolated to the
+    whole run (ceil(sum(prompt)/512) prefill steps + (new_tokens) decode steps)."""
+    from oracle.engine import OracleCache, OracleLlama
+
+    torch.set_num_threads(threads)
+    cfg = llama_1b_config()
+    config = dict(hidden_size=cfg.hidden_size, q_head_num=cfg.q_head_num, kv_head_num=cfg.kv_head_num,
+                  num_layers=cfg.num_layers, norm_eps=cfg.norm_eps, rope_theta=cfg.rope_theta, rope_type="llama3")
+    model = OracleLlama(model_cpu_state, config)
+    lens = [p.shape[1] for p in prompts]
+    blocks = sum(-(-(n + 1) // 16) for n in lens) + 64
+    cache = OracleCache(blocks, 16, cfg.num_layers, 8, 64, torch.bfloat16)
+    ids = [f"r{i}" for i in range(len(prompts))]
+    # contexts as if each prompt were already cached (values do not affect time)
+    for s, n in zip(ids, lens):
+        cache.tables.ensure_capacity(s, n)
+        cache.tables.advance(s, n)
+    with torch.inference_mode():
+        # one prefill step: 4 chunks of 128 tokens at the first 4 requests' contexts
+        t0 = time.perf_counter()
+        pf_ids = ids[:4]
+        model.forward_ragged(torch.randint(0, 128256, (512,)), pf_ids, [128] * 4, cache, last_only=True)
+        t_pf = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        model.forward_ragged(torch.randint(0, 128256, (len(ids),)), ids, [1] * len(ids), cache, last_only=True)
+        t_dec = time.perf_counter() - t0
+    return t_pf, t_dec
+
+
+def cpu_baseline(prompts, new_tokens, state):
+    threads = os.cpu_count() or 1
+    t_pf, t_dec = cpu_sample(prompts, state, threads)
+    n_pf = math.ceil(sum(p.shape[1] for p in prompts) / 512)
+    total = n_pf * t_pf + new_tokens * t_dec
+    tokens = len(prompts) * new_tokens
+    return {
+        "value": tokens / total,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": (f"oracle forward on host: one 512-token prefill step ({t_pf:.2f}s) and one "
+                   f"{len(prompts)}-token decode step ({t_dec:.2f}s) at the workload's contexts; "
+                   f"extrapolated to {n_pf} prefill + {new_tokens} decode steps"),
+    }
+
+
+def cpu_state_for_oracle():
+    from nano_infer_engine_b200.models.llama import build_random_llama
+
+    model = build_random_llama(llama_1b_config(), SEED, 0.02, torch.bfloat16, "cpu")
+    return dict(model.state_dict())
+
+
+# --------------------------------------------------------------- dist
+def init_dist(n):
+    if n <= 1 or "RANK" not in os.environ:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    return dist
+
+
+def barrier(dist_ctx):
+    if dist_ctx is not None:
+        dist_ctx.barrier()
+
+
+def max_over_ranks(dist_ctx, value, device):
+    if dist_ctx is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist_ctx.all_reduce(t, op=dist_ctx.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------ reference
+def run_reference(args):
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return 0
+    prompts = workload(args.requests)
+    state = cpu_state_for_oracle()
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_sample(prompts, state, threads)
+    values = []
+    t_start = time.perf_counter()
+    for _ in range(args.steps):
+        t_pf, t_dec = cpu_sample(prompts, state, threads)
+        n_pf = math.ceil(sum(p.shape[1] for p in prompts) / 512)
+        values.append(len(prompts) * args.new_tokens / (n_pf * t_pf + args.new_tokens * t_dec))
+    wall = time.perf_counter() - t_start
+    value = statistics.median(values)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": wall / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded prompts, random-init weights std 0.02)",
+        "config": {"workload": "config2: Llama-3.2-1B, 16 req, prompts U[128,2048], 256 new, chunk 128/512",
+                   "sample": "per step: one 512-token prefill step + one decode step, extrapolated"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": "oracle port of the reference forward on the host cores"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ------------------------------------------------------------------ main
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    dist_ctx = init_dist(args.gpus)
+    rank = int(os.environ.get("RANK", 0))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    import __graft_entry__
+
+    if rank == 0 or dist_ctx is None:
+        __graft_entry__.build()
+    barrier(dist_ctx)
+    if args.only == "decode":
+        dec = decode_config3(device, args.decode_iters, args.decode_batch, args.decode_blocks)
+        peak, _ = measured_peaks()
+        gbs = dec["bytes"] / (dec["ms"] / 1e3) / 1e9
+        print(json.dumps({"decode_ms": dec["ms"], "algorithmic_bytes": dec["bytes"], "GB/s": gbs,
+                          "frac": gbs / peak, "batch": dec["batch"], "sum_ctx": dec["sum_ctx"]}))
+        return 0
+    model = build_engine(device)
+    host_prompts = [p.pin_memory() for p in workload(args.requests)]
+    prompts = [p.to(device) for p in host_prompts]
+    cache = make_cache(device, args.requests, 2048 + args.new_tokens)
+
+    with ClockSampler(local) as clocks:
+        elapsed, launches = time_engine(model, cache, prompts, args.new_tokens, args.steps, args.warmup, dist_ctx)
+    elapsed = max_over_ranks(dist_ctx, elapsed, device)
+    world = dist_ctx.get_world_size() if dist_ctx else 1
+    tokens = args.requests * args.new_tokens * args.steps * world
+    value = tokens / elapsed
+
+    e2e = None
+    if not args.no_e2e:
+        e2e_s, h2d, d2h = time_e2e(model, cache, host_prompts, args.new_tokens, max(1, args.steps // 2), device)
+        e2e_s = max_over_ranks(dist_ctx, e2e_s, device)
+        e2e = {"value": args.requests * args.new_tokens * max(1, args.steps // 2) * world / e2e_s, "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+    del cache
+    torch.cuda.empty_cache()
+    if args.only == "engine":
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "e2e": e2e, "gpu_launches": launches,
+                              "ms_per_step": elapsed / args.steps * 1e3, "clocks": clocks.summary()}))
+        return 0
+    dec = decode_config3(device, args.decode_iters, args.decode_batch, args.decode_blocks)
+    peak, peak_kind = measured_peaks()
+    achieved = dec["bytes"] / (dec["ms"] / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": ncu_traffic(), "kernel": "decode_tma_kernel + decode_combine_kernel",
+                "workload": f"config3 decode: B=64, sum ctx {dec['sum_ctx']}, {dec['bytes']} algorithmic bytes/launch",
+                "ms_per_launch": dec["ms"], "peak_kind": f"{peak_kind} (hbm_gbs burst copy)"}
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        del model
+        torch.cuda.empty_cache()
+        cpu = cpu_baseline(workload(args.requests), args.new_tokens, cpu_state_for_oracle())
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps * 1e3,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded prompts, random-init weights N(0, 0.02))",
+            "config": {
+                "workload": "config2: Llama-3.2-1B shape, 16 requests, prompts U[128,2048], 256 greedy new "
+                            "tokens, prefill chunk 128, <=512 prefill tokens/step, block 16, max_model_len 29600",
+                "global_batch": args.requests * world,
+                "parallelism": f"replicas x{world}",
+                "l2": "inputs larger than L2 (2.47 GB of weights streamed per decode step)",
+            },
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line))
+    if dist_ctx is not None:
+        dist_ctx.barrier()
+        dist_ctx.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -182,9 +182,14 @@ int nie_paged_decode(const void* q, int64_t q_row_stride, void* out,
  * the cache (nie_write_kv).  For request r = req_list[i] (or i), its query
  * tokens are rows [query_start_loc[r], query_start_loc[r+1]) of q/out; the
  * token at offset j has position seq_lens[r] - qlen + j and attends to cached
- * positions [0, position].
+ * positions [0, position].  q/out hold num_q_rows rows of [q_heads,
+ * head_dim] at `row_stride` elements.
+ *
+ * bf16 / head_dim 64 / block_size 16 runs on the tcgen05 tensor cores (S and
+ * O accumulate in TMEM, K/V tiles arrive by TMA); other shapes use the
+ * generic kernel.
  */
-int nie_varlen_attention(const void* q, void* out, int64_t row_stride,
+int nie_varlen_attention(const void* q, void* out, int64_t row_stride, int64_t num_q_rows,
                          const void* key_cache, const void* value_cache,
                          int32_t dtype, int32_t layer, int64_t num_layers,
                          int64_t num_blocks, int32_t block_size, int32_t kv_heads,

@@ -23,6 +23,7 @@ SOURCES = (
     "nie_meta.cu",
     "nie_attn_generic.cu",
     "nie_attn_decode.cu",
+    "nie_attn_prefill.cu",
 )
 
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")

@@ -62,7 +62,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "nie_varlen_attention": (
         c_int,
-        [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int32, c_int64, c_int64]
+        [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int32, c_int32, c_int64, c_int64]
         + [c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]
         + [c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p],
     ),

@@ -29,6 +29,13 @@ struct GenericArgs {
 // Launch the generic kernel over grid (num_req, max_q, q_heads).
 int launch_generic(int dtype, const GenericArgs& a, int num_req, int max_q, cudaStream_t s);
 
+// tcgen05 varlen kernel (nie_attn_prefill.cu); NIE_ERR_UNSUPPORTED = use the generic one.
+int launch_prefill_tc(const void* q, void* out, int64_t row_stride, int64_t num_q_rows, const void* key_cache,
+                      const void* value_cache, int32_t layer, int64_t num_blocks, int32_t kv_heads, int32_t q_heads,
+                      const int32_t* block_tables, int64_t table_stride, const int32_t* table_rows,
+                      const int32_t* seq_lens, const int64_t* qsl, const int32_t* req_list, int32_t num_requests,
+                      int32_t max_query_len, float scale, int32_t* err_flag, cudaStream_t s);
+
 // Build the per-layer 3-D tensor map used by the TMA kernels: dims
 // {head_dim, kv_heads, num_blocks * block_size}, box {head_dim, 1, block_size},
 // 128-byte swizzle.

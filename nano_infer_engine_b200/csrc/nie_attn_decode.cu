@@ -541,7 +541,8 @@ extern "C" int nie_paged_decode(const void* q, int64_t q_row_stride, void* out, 
   return check_launch("decode_combine_kernel");
 }
 
-extern "C" int nie_varlen_attention(const void* q, void* out, int64_t row_stride, const void* key_cache,
+extern "C" int nie_varlen_attention(const void* q, void* out, int64_t row_stride, int64_t num_q_rows,
+                                    const void* key_cache,
                                     const void* value_cache, int32_t dtype, int32_t layer, int64_t num_layers,
                                     int64_t num_blocks, int32_t block_size, int32_t kv_heads, int32_t head_dim,
                                     int32_t q_heads, const int32_t* block_tables, int64_t table_stride,
@@ -555,8 +556,15 @@ extern "C" int nie_varlen_attention(const void* q, void* out, int64_t row_stride
   NIE_REQUIRE(num_blocks > 0 && block_size > 0 && kv_heads > 0 && head_dim > 0 && q_heads > 0, "bad geometry");
   NIE_REQUIRE(q_heads % kv_heads == 0, "q_heads must be divisible by kv_heads");
   NIE_REQUIRE(num_requests >= 0, "num_requests must be non-negative");
+  NIE_REQUIRE(num_q_rows >= 0, "num_q_rows must be non-negative");
   if (num_requests == 0) return NIE_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == NIE_DTYPE_BF16 && head_dim == 64 && block_size == 16 && max_query_len > 0) {
+    const int rc = launch_prefill_tc(q, out, row_stride, num_q_rows, key_cache, value_cache, layer, num_blocks,
+                                     kv_heads, q_heads, block_tables, table_stride, table_rows, seq_lens,
+                                     query_start_loc, req_list, num_requests, max_query_len, scale, err_flag, s);
+    if (rc != NIE_ERR_UNSUPPORTED) return rc;
+  }
   GenericArgs ga{};
   ga.q = q;
   ga.out = out;

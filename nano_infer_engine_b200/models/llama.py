@@ -128,6 +128,19 @@ def init_random_weights_(model: nn.Module, seed: int, std: float = 0.02) -> nn.M
     return model
 
 
+def build_random_llama(
+    config: "LlamaConfig", seed: int, std: float = 0.02, dtype: torch.dtype = torch.float32, device="cpu"
+) -> "Llama3_2":
+    """Allocate without default init, fill with :func:`init_random_weights_`, move to device."""
+    with torch.device("meta"):
+        model = Llama3_2(config)
+    model = model.to_empty(device="cpu")
+    if config.tie_word_embeddings:
+        model.lm_head.weight = model.embed.weight
+    init_random_weights_(model, seed, std)
+    return model.to(dtype=dtype, device=device).eval()
+
+
 class Llama3_2(nn.Module):
     """Reference models/llama.py:95-394 module tree and entry points."""
 

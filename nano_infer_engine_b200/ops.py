@@ -55,6 +55,16 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+# Number of kernels this process has launched through the library (the fast
+# decode path is two kernels: the split-K pass and the combine pass).
+LAUNCHES = 0
+
+
+def _count(n: int = 1) -> None:
+    global LAUNCHES
+    LAUNCHES += n
+
+
 # ------------------------------------------------------------ device errors
 _err_flags: dict[int, torch.Tensor] = {}
 
@@ -162,6 +172,7 @@ def pack_ragged(
         _stream(device),
     )
     check(status, "nie_pack_ragged")
+    _count()
     return RaggedMeta(
         query_start_loc=qsl,
         positions=positions,
@@ -228,6 +239,7 @@ def write_kv(
         _stream(device),
     )
     check(status, "nie_write_kv")
+    _count()
 
 
 def gather_kv(
@@ -263,6 +275,7 @@ def gather_kv(
         _stream(device),
     )
     check(status, "nie_gather_kv")
+    _count()
     return out_k, out_v
 
 
@@ -314,6 +327,7 @@ def copy_blocks(
             _stream(run_device),
         )
     check(status, "nie_copy_blocks")
+    _count()
 
 
 _peer_enabled: set[tuple[int, int]] = set()
@@ -403,6 +417,8 @@ def paged_decode(
         _stream(device),
     )
     check(status, "nie_paged_decode")
+    fast = query.dtype == torch.bfloat16 and d == 64 and bs == 16 and hq // h <= 16 and h <= 16
+    _count(2 if fast else 1)
     return out
 
 
@@ -440,6 +456,7 @@ def varlen_attention(
         query.data_ptr(),
         out.data_ptr(),
         query.stride(0),
+        query.shape[0],
         key_cache.data_ptr(),
         value_cache.data_ptr(),
         dtype_code(query.dtype),
@@ -463,4 +480,5 @@ def varlen_attention(
         _stream(device),
     )
     check(status, "nie_varlen_attention")
+    _count()
     return out

@@ -249,3 +249,82 @@ def test_varlen_against_oracle(cuda, dtype):
     ops().check_device_errors(cuda)
     want = oatt.varlen_attention(q, kc, vc, tables, contexts, qlens, 1)
     torch.testing.assert_close(out.cpu().float(), want.float(), atol=TOL[dtype], rtol=0)
+
+
+@pytest.mark.parametrize("seed,contexts,qlens", [
+    (30, [0, 0, 5], [1, 2, 17]),
+    (31, [0, 130, 4000, 8100, 37], [128, 128, 128, 128, 300]),
+    (32, [0], [1000]),
+    (33, [15, 16, 17, 255, 256, 257], [2, 16, 127, 129, 3, 64]),
+])
+def test_tensor_core_varlen_against_oracle(cuda, seed, contexts, qlens):
+    """tcgen05 path (bf16, hd 64, bs 16): multi-tile queries, long contexts, ragged
+    ends; stale rows past each sequence end hold NaN and must not leak."""
+    g = torch.Generator().manual_seed(seed)
+    bs, hkv, hq = 16, 8, 32
+    lens = [c + q for c, q in zip(contexts, qlens)]
+    nb = sum((n + bs - 1) // bs for n in lens) + 5
+    tables = _random_layout(nb, lens, bs, seed)
+    kc = torch.randn(1, nb, bs, hkv, 64, generator=g).to(torch.bfloat16)
+    vc = torch.randn(1, nb, bs, hkv, 64, generator=g).to(torch.bfloat16)
+    q = torch.randn(sum(qlens), hq, 64, generator=g).to(torch.bfloat16)
+    dk, dv = kc.to(cuda), vc.to(cuda)
+    for t, n in zip(tables, lens):
+        if n % bs:
+            dk[0, t[-1], n % bs:] = float("nan")
+            dv[0, t[-1], n % bs:] = float("nan")
+    qsl = [0]
+    for n in qlens:
+        qsl.append(qsl[-1] + n)
+    out = ops().varlen_attention(q.to(cuda), dk, dv, 0, _tables_tensor(tables, cuda),
+                                 torch.tensor(lens, dtype=torch.int32, device=cuda),
+                                 torch.tensor(qsl, dtype=torch.int64, device=cuda), max(qlens))
+    ops().check_device_errors(cuda)
+    want = oatt.varlen_attention(q, kc, vc, tables, contexts, qlens, 0)
+    got = out.cpu().float()
+    assert torch.isfinite(got).all()
+    torch.testing.assert_close(got, want.float(), atol=2e-2, rtol=0)
+
+
+def test_mixed_step_config4_shape(cuda):
+    """BASELINE config 4 at reduced context: 8 prefill chunks of 128 + 120 decode rows,
+    prefill first, through pack -> write -> decode + varlen, against the oracle."""
+    g = torch.Generator().manual_seed(40)
+    bs, hkv, hq = 16, 8, 32
+    pf_ctx = torch.randint(0, 2048, (8,), generator=g).tolist()
+    dec_ctx = torch.randint(256, 4096, (120,), generator=g).tolist()
+    contexts = pf_ctx + dec_ctx
+    qlens = [128] * 8 + [1] * 120
+    lens = [c + q for c, q in zip(contexts, qlens)]
+    nb = sum((n + bs - 1) // bs for n in lens) + 3
+    tables = _random_layout(nb, lens, bs, 40)
+    kc = torch.randn(1, nb, bs, hkv, 64, generator=g).to(torch.bfloat16)
+    vc = torch.randn(1, nb, bs, hkv, 64, generator=g).to(torch.bfloat16)
+    T = sum(qlens)
+    q = torch.randn(T, hq, 64, generator=g).to(torch.bfloat16)
+    k_new = torch.randn(T, hkv, 64, generator=g).to(torch.bfloat16)
+    v_new = torch.randn(T, hkv, 64, generator=g).to(torch.bfloat16)
+    R = len(qlens)
+    plan = torch.tensor([list(range(R)), contexts, qlens], dtype=torch.int32).to(cuda)
+    meta = ops().pack_ragged(plan, T, _tables_tensor(tables, cuda), bs, nb, num_decode=120, max_query_len=128)
+    dk, dv = kc.to(cuda), vc.to(cuda)
+    qd = q.to(cuda)
+    ops().write_kv(k_new.to(cuda), v_new.to(cuda), dk, dv, 0, meta.slot_mapping)
+    out = torch.empty_like(qd)
+    ops().paged_decode(qd, dk, dv, 0, meta.block_tables, meta.seq_lens, out=out, table_rows=meta.table_rows,
+                       q_rows=meta.query_start_loc, req_list=meta.decode_list, num_requests=meta.num_decode)
+    ops().varlen_attention(qd, dk, dv, 0, meta.block_tables, meta.seq_lens, meta.query_start_loc, 128, out=out,
+                           table_rows=meta.table_rows, req_list=meta.prefill_list, num_requests=meta.num_prefill)
+    ops().check_device_errors(cuda)
+    # oracle: write the new rows on the CPU copy, then attend
+    kc2, vc2 = kc.clone(), vc.clone()
+    pos = 0
+    for t, c, ql in zip(tables, contexts, qlens):
+        for j in range(ql):
+            p = c + j
+            kc2[0, t[p // bs], p % bs] = k_new[pos]
+            vc2[0, t[p // bs], p % bs] = v_new[pos]
+            pos += 1
+    assert torch.equal(dk.cpu(), kc2) and torch.equal(dv.cpu(), vc2)
+    want = oatt.varlen_attention(q, kc2, vc2, tables, contexts, qlens, 0)
+    torch.testing.assert_close(out.cpu().float(), want.float(), atol=2e-2, rtol=0)
