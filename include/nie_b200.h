@@ -173,6 +173,47 @@ int nie_paged_decode(const void* q, int64_t q_row_stride, void* out,
                      size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 /*
+ * Allocation-free paged decode.  This entry point has no counterpart in the
+ * reference engine; it exists for callers that cannot allocate device memory:
+ * code that binds this C ABI from a host language with no device allocator of
+ * its own (a cgo, JNI or plain ctypes binding that only holds the buffers it
+ * was handed), or an embedding runtime that owns all device memory through its
+ * own pool and must not see extra cudaMalloc/cudaFree calls (which can also
+ * stall a serving loop by synchronizing the device).
+ *
+ * Same arguments and results as nie_paged_decode, minus the workspace: the
+ * split-K scratch is a fixed array of NIE_DECODE_NOALLOC_SCRATCH_BYTES inside
+ * the library, which every GPU that loads the library holds until the process
+ * exits.  The caller still passes q, out, the caches, tables and lengths.
+ *  - Limit: the call must fit the array, i.e.
+ *    nie_paged_decode_workspace_size(...) <= NIE_DECODE_NOALLOC_SCRATCH_BYTES
+ *    (about 840 requests at 32 query heads on a 148-SM B200); larger calls
+ *    fail with NIE_ERR_INVALID and a message naming the limit.
+ *  - The first call on a device looks up the array's device address with that
+ *    device current; make that first call before any stream capture.
+ *  - Every call shares the one array, which keeps the last call's contents
+ *    (the kernels need no zeroed scratch).  Calls that overlap on the GPU
+ *    (several streams or host threads at once) race on it: serialize them.
+ *  - Nothing is allocated: no cudaMalloc, cudaFree or allocating library call.
+ */
+#define NIE_DECODE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+
+/* Size in bytes of the fixed scratch array (NIE_DECODE_NOALLOC_SCRATCH_BYTES). */
+size_t nie_paged_decode_noalloc_capacity(void);
+
+int nie_paged_decode_noalloc(const void* q, int64_t q_row_stride, void* out,
+                             int64_t out_row_stride, const void* key_cache,
+                             const void* value_cache, int32_t dtype,
+                             int32_t layer, int64_t num_layers,
+                             int64_t num_blocks, int32_t block_size,
+                             int32_t kv_heads, int32_t head_dim,
+                             int32_t q_heads, const int32_t* block_tables,
+                             int64_t table_stride, const int32_t* table_rows,
+                             const int32_t* seq_lens, const int64_t* q_rows,
+                             const int32_t* req_list, int32_t num_requests,
+                             float scale, int32_t* err_flag, void* stream);
+
+/*
  * (d) Varlen causal attention over the paged cache (chunked prefill, and the
  * prefill rows of a mixed step).  Replaces the per-request write/gather/
  * attention loop of GroupedQueryAttention.forward_ragged

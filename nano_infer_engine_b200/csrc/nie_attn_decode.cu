@@ -25,6 +25,8 @@
 // product as bf16 and the output is rounded once.  The one difference from
 // the reference is that p is normalised after the PV product instead of
 // before its cast to bf16 (online softmax), a < 2^-8 relative effect.
+#include <mutex>
+
 #include "nie_attn.cuh"
 
 namespace nie {
@@ -588,4 +590,69 @@ extern "C" int nie_varlen_attention(const void* q, void* out, int64_t row_stride
   ga.scale = scale;
   ga.err = err_flag;
   return launch_generic(dtype, ga, num_requests, max_query_len, s);
+}
+
+// ------------------------------------------------- allocation-free decode
+// Scratch of nie_paged_decode_noalloc: a fixed array in device memory that
+// every GPU loading this library holds until the process exits.  Host code
+// must never hand this symbol to a kernel directly (on the host it is only a
+// stand-in, not a device address); the address comes from
+// cudaGetSymbolAddress, resolved once per device below.
+static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[NIE_DECODE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+// Resolve the device address of the scratch array on `device`, which must be
+// the current device.  Runs once per device (the first call on that device).
+int noalloc_scratch(int device, void** out) {
+  if (device < 0 || device >= 64) return nie::fail(NIE_ERR_INVALID, "device %d out of range", device);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[device] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return nie::fail(NIE_ERR_CUDA, "cudaGetSymbolAddress(decode scratch) on device %d: %s", device,
+                       cudaGetErrorString(e));
+    g_noalloc_ptr[device] = p;
+  }
+  *out = g_noalloc_ptr[device];
+  return NIE_OK;
+}
+}  // namespace
+
+extern "C" size_t nie_paged_decode_noalloc_capacity(void) { return NIE_DECODE_NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int nie_paged_decode_noalloc(const void* q, int64_t q_row_stride, void* out, int64_t out_row_stride,
+                                        const void* key_cache, const void* value_cache, int32_t dtype, int32_t layer,
+                                        int64_t num_layers, int64_t num_blocks, int32_t block_size, int32_t kv_heads,
+                                        int32_t head_dim, int32_t q_heads, const int32_t* block_tables,
+                                        int64_t table_stride, const int32_t* table_rows, const int32_t* seq_lens,
+                                        const int64_t* q_rows, const int32_t* req_list, int32_t num_requests,
+                                        float scale, int32_t* err_flag, void* stream) {
+  NIE_REQUIRE(num_requests >= 0 && q_heads > 0, "num_requests must be non-negative and q_heads positive");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int dev = stream_device(s);
+  const int sms = sm_count(dev);
+  NIE_REQUIRE(sms > 0, "cannot query the SM count of device %d", dev);
+  if (num_requests > 0) {
+    const size_t need = ws_bytes(sms * kDecCtasPerSm, num_requests, q_heads);
+    if (need > (size_t)NIE_DECODE_NOALLOC_SCRATCH_BYTES)
+      return fail(NIE_ERR_INVALID,
+                  "nie_paged_decode_noalloc: %d requests x %d query heads need %zu bytes of scratch, above the "
+                  "fixed %d-byte array; use nie_paged_decode with a caller-provided workspace",
+                  num_requests, q_heads, need, NIE_DECODE_NOALLOC_SCRATCH_BYTES);
+  }
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) return fail(NIE_ERR_CUDA, "cudaGetDevice failed");
+  if (prev != dev && cudaSetDevice(dev) != cudaSuccess) return fail(NIE_ERR_CUDA, "cudaSetDevice(%d) failed", dev);
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(dev, &scratch);
+  if (prev != dev) cudaSetDevice(prev);
+  if (rc != NIE_OK) return rc;
+  return nie_paged_decode(q, q_row_stride, out, out_row_stride, key_cache, value_cache, dtype, layer, num_layers,
+                          num_blocks, block_size, kv_heads, head_dim, q_heads, block_tables, table_stride, table_rows,
+                          seq_lens, q_rows, req_list, num_requests, scale, scratch,
+                          (size_t)NIE_DECODE_NOALLOC_SCRATCH_BYTES, err_flag, stream);
 }
