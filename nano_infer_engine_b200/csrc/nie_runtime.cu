@@ -49,12 +49,13 @@ int sm_count(int device) {
   return g_sm_count[device];
 }
 
+// Device whose SMs a launch on `stream` uses.  A kernel launch requires the
+// stream to belong to the current device, so the current device is the
+// answer; querying the stream itself (cudaStreamGetDevice) would invalidate a
+// CUDA-graph capture in progress on it.
 int stream_device(cudaStream_t stream) {
+  (void)stream;
   int dev = -1;
-  if (stream != nullptr) {
-    if (cudaStreamGetDevice(stream, &dev) == cudaSuccess) return dev;
-    cudaGetLastError();
-  }
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
   return dev;
 }

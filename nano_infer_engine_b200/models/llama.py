@@ -141,8 +141,55 @@ def build_random_llama(
     return model.to(dtype=dtype, device=device).eval()
 
 
+class _DecodeGraph:
+    """A captured decode-only step (every request has one query token) for a fixed batch.
+
+    The plan (table rows, contexts, query lengths) and token ids live in
+    static device buffers that are refreshed before each replay; the packing
+    kernel, all layers and the lm_head run inside the graph.  A graph is tied
+    to one cache and one block-table tensor (the table is reallocated when it
+    grows, which retires the graph).
+    """
+
+    def __init__(self, model: "Llama3_2", cache: PagedKVCache, batch: int) -> None:
+        dev = cache.device
+        self.batch = batch
+        # the graph bakes in raw pointers: keep every buffer it touches alive
+        self.model = model
+        self.workspace = ops.decode_workspace(dev, batch, model.config.q_head_num, model.config.head_dim)
+        self.ids = torch.zeros(batch, dtype=torch.long, device=dev)
+        self.plan = torch.zeros((3, batch), dtype=torch.int32, device=dev)
+        self.table = cache.device_block_tables()
+        self.graph = torch.cuda.CUDAGraph()
+        launches = ops.LAUNCHES
+        with torch.cuda.graph(self.graph):
+            meta = ops.pack_ragged(
+                self.plan,
+                batch,
+                self.table,
+                cache.block_size,
+                cache.allocator.num_blocks,
+                num_decode=batch,
+                max_query_len=1,
+            )
+            self.logits = model.run_ragged(self.ids, meta, cache)
+        # library kernels inside the graph, counted again at every replay
+        self.kernels = ops.LAUNCHES - launches
+        ops.LAUNCHES = launches
+
+    def run(self, input_ids: torch.Tensor, plan_host: torch.Tensor) -> torch.Tensor:
+        self.plan.copy_(plan_host.pin_memory(), non_blocking=True)
+        self.ids.copy_(input_ids)
+        self.graph.replay()
+        ops._count(self.kernels)
+        return self.logits.clone()
+
+
 class Llama3_2(nn.Module):
     """Reference models/llama.py:95-394 module tree and entry points."""
+
+    # Replay decode-only steps from captured CUDA graphs (one per batch size).
+    cuda_graphs: bool = True
 
     def __init__(self, config: LlamaConfig) -> None:
         super().__init__()
@@ -187,6 +234,43 @@ class Llama3_2(nn.Module):
             x = x.index_select(0, logit_rows)
         return self.lm_head(self.final_rms(x))
 
+    def _decode_step(
+        self,
+        input_ids: torch.Tensor,
+        cache: PagedKVCache,
+        sequence_ids: tuple[str, ...],
+        context_lengths: tuple[int, ...],
+    ) -> torch.Tensor:
+        """One decode-only step ([R] ids -> [R, vocab] logits), replayed from a CUDA graph.
+
+        The first step of a given batch size runs eagerly (it doubles as the
+        warm-up) and then captures the graph used by later steps.  Graphs are
+        stored on the cache, so they die with it.
+        """
+        batch = len(sequence_ids)
+        table = cache.device_block_tables()
+        graphs = cache.__dict__.setdefault("_decode_graphs", {})
+        key = (id(self), batch)
+        graph = graphs.get(key)
+        if graph is not None and graph.table is not table:
+            graph = None  # the block-table tensor was reallocated
+        if graph is None:
+            meta = cache.pack(sequence_ids, context_lengths, (1,) * batch)
+            logits = self.run_ragged(input_ids, meta, cache)
+            graphs[key] = _DecodeGraph(self, cache, batch)
+            return logits
+        rows = [cache.table_row(s) for s in sequence_ids]
+        plan = torch.tensor([rows, list(context_lengths), [1] * batch], dtype=torch.int32)
+        return graph.run(input_ids, plan)
+
+    def _use_graph(self, cache: PagedKVCache, query_lengths) -> bool:
+        return (
+            self.cuda_graphs
+            and cache.device.type == "cuda"
+            and all(q == 1 for q in query_lengths)
+            and not torch.cuda.is_current_stream_capturing()
+        )
+
     # -------------------------------------------------------- ragged entry
     def forward_ragged(
         self,
@@ -222,11 +306,15 @@ class Llama3_2(nn.Module):
                 raise ValueError(f"Sequence length {c + q} exceeds max_seq_len={self.config.max_seq_len}")
             kv_cache.ensure_capacity(s, c + q)
 
-        meta = kv_cache.pack(tuple(sequence_ids), context_lengths, query_lengths)
         last_only = bool(getattr(query_start_loc, LAST_ROWS_ONLY, False))
-        logits = self.run_ragged(
-            input_ids, meta, kv_cache, logit_rows=meta.last_token_index if last_only else None
-        )
+        if self._use_graph(kv_cache, query_lengths):
+            # every row is its request's last row: full and last-row logits coincide
+            logits = self._decode_step(input_ids, kv_cache, tuple(sequence_ids), context_lengths)
+        else:
+            meta = kv_cache.pack(tuple(sequence_ids), context_lengths, query_lengths)
+            logits = self.run_ragged(
+                input_ids, meta, kv_cache, logit_rows=meta.last_token_index if last_only else None
+            )
         for s, q in zip(sequence_ids, query_lengths):
             kv_cache.advance(s, q)
         if last_only:
@@ -316,6 +404,11 @@ class Llama3_2(nn.Module):
                     raise ValueError("position_ids must be on the same device as x")
                 rope_positions = position_ids.reshape(-1)
 
+        if decode and position_ids is None and self._use_graph(kv_cache, (1,) * batch):
+            logits = self._decode_step(x.reshape(-1), kv_cache, ids, lengths)
+            for s in ids:
+                kv_cache.advance(s, 1)
+            return logits.view(batch, 1, -1)
         meta = kv_cache.pack(ids, lengths, (seq_len,) * batch)
         last_only = bool(getattr(x, LAST_ROWS_ONLY, False))
         logits = self.run_ragged(

@@ -134,7 +134,43 @@ def config1() -> dict:
     }
 
 
+def config2_reduced() -> dict:
+    """BASELINE config 2 (Llama-3.2-1B shape, bf16, random init std 0.02) with the
+    bench's seeded workload but only CONFIG2_NEW_TOKENS new tokens per request."""
+    from nano_infer_engine_b200.models.llama import LlamaConfig as OurConfig, build_random_llama
+
+    ours = build_random_llama(OurConfig(max_seq_len=29600), recipes.CONFIG2_WEIGHT_SEED, 0.02, torch.bfloat16, "cpu")
+    model = Llama3_2(LlamaConfig(max_seq_len=29600)).to(torch.bfloat16).eval()
+    model.load_state_dict(ours.state_dict())
+    del ours
+    prompts = recipes.config2_prompts()
+    blocks = sum((p.shape[1] + recipes.CONFIG2_NEW_TOKENS + 15) // 16 for p in prompts) + 16
+    cache = PagedKVCache(blocks, 16, 16, 8, 64, torch.bfloat16, "cpu")
+    config = GenerationConfig(max_new_tokens=recipes.CONFIG2_NEW_TOKENS, prefill_chunk_size=128,
+                              max_prefill_tokens_per_step=512)
+    sched = ContinuousBatchingScheduler(model, config, cache, len(prompts))
+    ids = [f"req-{i}" for i in range(len(prompts))]
+    reqs = [sched.add_request(s, p) for s, p in zip(ids, prompts)]
+    # margin (top-1 minus top-2 logit) of every greedy decision, read from the
+    # logits each active request holds right before the step that samples it
+    margins: dict[str, list[float]] = {s: [] for s in ids}
+    with torch.inference_mode():
+        while sched.has_work:
+            for r in sched.active_requests:
+                top2 = r.last_logits.float().topk(2).values
+                margins[r.sequence_id].append(float(top2[0] - top2[1]))
+            sched.step()
+    return {
+        "tokens": {r.sequence_id: r.sequence[0, r.prompt.shape[1]:].tolist() for r in reqs},
+        "margins": margins,
+    }
+
+
 def main() -> None:
+    if "--config2" in sys.argv:
+        (HERE / "config2_tokens.json").write_text(json.dumps(config2_reduced()))
+        print("config2 golden written")
+        return
     (HERE / "paging.json").write_text(json.dumps(paging(), indent=1))
     for name in recipes.DECODE_CASES:
         torch.save(decode(name), HERE / f"decode_{name}.pt")

@@ -103,3 +103,14 @@ def config1_prompts() -> list[torch.Tensor]:
 
 CONFIG1_WEIGHT_SEED = 0
 CONFIG1_STD = 0.02
+
+# BASELINE config 2 (Llama-3.2-1B shape, bf16): the bench's seeded workload
+CONFIG2_WEIGHT_SEED = 1234
+CONFIG2_NEW_TOKENS = 8
+
+
+def config2_prompts(num_requests: int = 16, seed: int = 1234) -> list[torch.Tensor]:
+    """16 prompts, lengths U[128, 2048], ids U[0, 128256) (same draw as bench.py)."""
+    g = torch.Generator().manual_seed(seed)
+    lengths = torch.randint(128, 2049, (num_requests,), generator=g).tolist()
+    return [torch.randint(0, 128256, (1, n), generator=g) for n in lengths]

@@ -94,3 +94,49 @@ def test_config1_greedy_tokens_and_step_plan_match_reference(cuda):
         assert got["qsl"] == want["qsl"]
         assert got["tables_after"] == want["tables_after"]
     assert cache.allocator.free_block_count == golden["free_blocks_after"]
+
+
+def _llama_shaped_model(cuda, seed=7):
+    """Llama attention geometry (head_dim 64, 4 q heads per kv head, bf16) at small width."""
+    from nano_infer_engine_b200.models.llama import LlamaConfig, build_random_llama
+
+    cfg = LlamaConfig(vocab_size=512, hidden_size=512, mlp_inner_size=1024, num_layers=2, q_head_num=8,
+                      kv_head_num=2, max_seq_len=4096)
+    return build_random_llama(cfg, seed, 0.02, torch.bfloat16, cuda), cfg
+
+
+def _generate(model, cfg, prompts, cuda, *, graphs, chunk):
+    from nano_infer_engine_b200.generation.config import GenerationConfig
+    from nano_infer_engine_b200.generation.scheduler import ContinuousBatchingScheduler
+    from nano_infer_engine_b200.paged_cache import PagedKVCache
+
+    model.cuda_graphs = graphs
+    cache = PagedKVCache(256, 16, cfg.num_layers, cfg.kv_head_num, cfg.head_dim, torch.bfloat16, cuda)
+    config = GenerationConfig(max_new_tokens=12, prefill_chunk_size=chunk, max_prefill_tokens_per_step=64 if chunk else None)
+    sched = ContinuousBatchingScheduler(model, config, cache, 4)
+    reqs = [sched.add_request(f"r{i}", p) for i, p in enumerate(prompts)]
+    logits = []
+    with torch.inference_mode():
+        while sched.has_work:
+            sched.step()
+            logits.extend(r.last_logits.float().cpu() for r in sched.active_requests if r.last_logits is not None)
+    return [r.sequence[0].tolist() for r in reqs], logits, cache
+
+
+@pytest.mark.parametrize("chunk", [32, None])
+def test_cuda_graph_decode_matches_eager(cuda, chunk):
+    """Decode steps replayed from CUDA graphs give the eager path's tokens and logits."""
+    from nano_infer_engine_b200 import ops
+
+    model, cfg = _llama_shaped_model(cuda)
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, cfg.vocab_size, (1, n), generator=g).to(cuda) for n in (5, 40, 77, 16, 130)]
+    eager_tokens, eager_logits, _ = _generate(model, cfg, prompts, cuda, graphs=False, chunk=chunk)
+    graph_tokens, graph_logits, cache = _generate(model, cfg, prompts, cuda, graphs=True, chunk=chunk)
+    ops.check_device_errors(cuda)
+    assert graph_tokens == eager_tokens
+    assert len(graph_logits) == len(eager_logits)
+    for a, b in zip(graph_logits, eager_logits):
+        torch.testing.assert_close(a, b, atol=1e-2, rtol=0)
+    assert getattr(cache, "_decode_graphs", None), "no decode step was captured"
+    assert cache.allocator.allocated_block_count == 0
