@@ -55,8 +55,9 @@ def parse_args():
     p.add_argument("--decode-iters", type=int, default=20)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--only", choices=("all", "engine", "decode"), default="all",
-                   help="engine: headline run only; decode: config-3 decode micro-bench only (profiling)")
+    p.add_argument("--only", choices=("all", "engine", "decode", "mixed"), default="all",
+                   help="engine: headline run only; decode: config-3 decode micro-bench only; "
+                        "mixed: config-4 mixed step only (profiling)")
     p.add_argument("--decode-batch", type=int, default=64)
     p.add_argument("--decode-blocks", type=int, default=131072)
     return p.parse_args()
@@ -239,6 +240,68 @@ def decode_config3(device, iters, B=64, nb=131072):
     return {"ms": ms, "bytes": algo_bytes, "sum_ctx": sum_ctx, "batch": B}
 
 
+def mixed_config4(device, iters):
+    """8 prefill chunks of 128 at ctx U[0, 8192] + 120 decode rows at
+    ctx U[256, 16384] (prefill first), one layer of the Llama-1B attention shape.
+    Times the tcgen05 varlen kernel and the decode kernel separately."""
+    from nano_infer_engine_b200 import ops
+
+    g = torch.Generator().manual_seed(4)
+    bs = 16
+    contexts = torch.randint(0, 8193, (8,), generator=g).tolist() + torch.randint(256, 16385, (120,), generator=g).tolist()
+    qlens = [128] * 8 + [1] * 120
+    lens = [c + q for c, q in zip(contexts, qlens)]
+    nb = sum(-(-n // bs) for n in lens) + 64
+    perm = torch.randperm(nb, generator=g)
+    width = max(-(-n // bs) for n in lens)
+    tables = torch.full((len(lens), width), -1, dtype=torch.int32)
+    at = 0
+    for i, n in enumerate(lens):
+        k = -(-n // bs)
+        tables[i, :k] = perm[at : at + k].to(torch.int32)
+        at += k
+    gen = torch.Generator(device=device).manual_seed(4)
+    kc = torch.randn((1, nb, bs, 8, 64), generator=gen, device=device, dtype=torch.bfloat16)
+    vc = torch.randn((1, nb, bs, 8, 64), generator=gen, device=device, dtype=torch.bfloat16)
+    T = sum(qlens)
+    q = torch.randn((T, 32, 64), generator=gen, device=device, dtype=torch.bfloat16)
+    R = len(lens)
+    plan = torch.tensor([list(range(R)), contexts, qlens], dtype=torch.int32).to(device)
+    meta = ops.pack_ragged(plan, T, tables.to(device), bs, nb, num_decode=120, max_query_len=128)
+    out = torch.empty_like(q)
+
+    def prefill():
+        ops.varlen_attention(q, kc, vc, 0, meta.block_tables, meta.seq_lens, meta.query_start_loc, 128, out=out,
+                             table_rows=meta.table_rows, req_list=meta.prefill_list, num_requests=8,
+                             max_seq_len=max(lens[:8]))
+
+    def decode():
+        ops.paged_decode(q, kc, vc, 0, meta.block_tables, meta.seq_lens, out=out, table_rows=meta.table_rows,
+                         q_rows=meta.query_start_loc, req_list=meta.decode_list, num_requests=120)
+
+    res = {}
+    for name, fn in (("prefill", prefill), ("decode", decode)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        res[name + "_ms"] = a.elapsed_time(b) / iters
+    ops.check_device_errors(device)
+    flops = sum(4 * 64 * 32 * (128 * c + 128 * 129 // 2) for c in contexts[:8])
+    dec_bytes = sum(lens[8:]) * 2048 + sum(-(-n // bs) for n in lens[8:]) * 4 + 2 * 120 * 32 * 64 * 2
+    res.update(prefill_flops=flops, prefill_tflops=flops / (res["prefill_ms"] / 1e3) / 1e12,
+               decode_bytes=dec_bytes, decode_gbs=dec_bytes / (res["decode_ms"] / 1e3) / 1e9,
+               prefill_contexts=contexts[:8])
+    del kc, vc
+    torch.cuda.empty_cache()
+    return res
+
+
 def measured_peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -404,6 +467,9 @@ def main():
         gbs = dec["bytes"] / (dec["ms"] / 1e3) / 1e9
         print(json.dumps({"decode_ms": dec["ms"], "algorithmic_bytes": dec["bytes"], "GB/s": gbs,
                           "frac": gbs / peak, "batch": dec["batch"], "sum_ctx": dec["sum_ctx"]}))
+        return 0
+    if args.only == "mixed":
+        print(json.dumps(mixed_config4(device, args.decode_iters)))
         return 0
     model = build_engine(device)
     host_prompts = [p.pin_memory() for p in workload(args.requests)]

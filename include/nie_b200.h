@@ -228,8 +228,14 @@ int nie_paged_decode_noalloc(const void* q, int64_t q_row_stride, void* out,
  *
  * bf16 / head_dim 64 / block_size 16 runs on the tcgen05 tensor cores (S and
  * O accumulate in TMEM, K/V tiles arrive by TMA); other shapes use the
- * generic kernel.
+ * generic kernel.  max_seq_len (host value, >= every seq_lens[r]; 0 =
+ * unknown) lets the tensor-core path split long key ranges over several CTAs;
+ * the split needs `workspace` of nie_varlen_workspace_size() bytes (scratch,
+ * no initialisation needed) and is skipped when it is NULL or too small.
  */
+size_t nie_varlen_workspace_size(int32_t num_requests, int32_t max_query_len,
+                                 int32_t max_seq_len, int32_t q_heads);
+
 int nie_varlen_attention(const void* q, void* out, int64_t row_stride, int64_t num_q_rows,
                          const void* key_cache, const void* value_cache,
                          int32_t dtype, int32_t layer, int64_t num_layers,
@@ -238,8 +244,9 @@ int nie_varlen_attention(const void* q, void* out, int64_t row_stride, int64_t n
                          const int32_t* block_tables, int64_t table_stride,
                          const int32_t* table_rows, const int32_t* seq_lens,
                          const int64_t* query_start_loc, const int32_t* req_list,
-                         int32_t num_requests, int32_t max_query_len, float scale,
-                         int32_t* err_flag, void* stream);
+                         int32_t num_requests, int32_t max_query_len,
+                         int32_t max_seq_len, float scale, void* workspace,
+                         size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 #ifdef __cplusplus
 }

@@ -34,7 +34,11 @@ int launch_prefill_tc(const void* q, void* out, int64_t row_stride, int64_t num_
                       const void* value_cache, int32_t layer, int64_t num_blocks, int32_t kv_heads, int32_t q_heads,
                       const int32_t* block_tables, int64_t table_stride, const int32_t* table_rows,
                       const int32_t* seq_lens, const int64_t* qsl, const int32_t* req_list, int32_t num_requests,
-                      int32_t max_query_len, float scale, int32_t* err_flag, cudaStream_t s);
+                      int32_t max_query_len, int32_t max_seq_len, float scale, void* workspace,
+                      size_t workspace_bytes, int32_t* err_flag, cudaStream_t s);
+
+// Scratch bytes the tcgen05 varlen kernel uses to split long key ranges.
+size_t prefill_workspace_bytes(int32_t num_requests, int32_t max_query_len, int32_t max_seq_len, int32_t q_heads);
 
 // Build the per-layer 3-D tensor map used by the TMA kernels: dims
 // {head_dim, kv_heads, num_blocks * block_size}, box {head_dim, 1, block_size},

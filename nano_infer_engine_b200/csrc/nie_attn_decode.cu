@@ -430,6 +430,11 @@ static size_t decode_smem_bytes(int hkv, int R) {
 
 using namespace nie;
 
+extern "C" size_t nie_varlen_workspace_size(int32_t num_requests, int32_t max_query_len, int32_t max_seq_len,
+                                            int32_t q_heads) {
+  return prefill_workspace_bytes(num_requests, max_query_len, max_seq_len, q_heads);
+}
+
 extern "C" size_t nie_paged_decode_workspace_size(int device, int32_t R, int32_t q_heads, int32_t head_dim) {
   const int sms = sm_count(device);
   if (sms <= 0 || R <= 0 || q_heads <= 0) return 0;
@@ -550,7 +555,8 @@ extern "C" int nie_varlen_attention(const void* q, void* out, int64_t row_stride
                                     int32_t q_heads, const int32_t* block_tables, int64_t table_stride,
                                     const int32_t* table_rows, const int32_t* seq_lens,
                                     const int64_t* query_start_loc, const int32_t* req_list, int32_t num_requests,
-                                    int32_t max_query_len, float scale, int32_t* err_flag, void* stream) {
+                                    int32_t max_query_len, int32_t max_seq_len, float scale, void* workspace,
+                                    size_t workspace_bytes, int32_t* err_flag, void* stream) {
   NIE_REQUIRE(dtype_size(dtype) > 0, "unknown dtype %d", dtype);
   NIE_REQUIRE(q && out && key_cache && value_cache && block_tables && seq_lens && query_start_loc,
               "null pointer argument");
@@ -564,7 +570,8 @@ extern "C" int nie_varlen_attention(const void* q, void* out, int64_t row_stride
   if (dtype == NIE_DTYPE_BF16 && head_dim == 64 && block_size == 16 && max_query_len > 0) {
     const int rc = launch_prefill_tc(q, out, row_stride, num_q_rows, key_cache, value_cache, layer, num_blocks,
                                      kv_heads, q_heads, block_tables, table_stride, table_rows, seq_lens,
-                                     query_start_loc, req_list, num_requests, max_query_len, scale, err_flag, s);
+                                     query_start_loc, req_list, num_requests, max_query_len, max_seq_len, scale,
+                                     workspace, workspace_bytes, err_flag, s);
     if (rc != NIE_ERR_UNSUPPORTED) return rc;
   }
   GenericArgs ga{};

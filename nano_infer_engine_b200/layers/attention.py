@@ -83,6 +83,7 @@ class GroupedQueryAttention(nn.Module):
                 table_rows=meta.table_rows,
                 req_list=meta.prefill_list,
                 num_requests=meta.num_prefill,
+                max_seq_len=meta.max_seq_len,
             )
         return self.o_proj(out.view(T, self.hidden_size))
 

@@ -119,6 +119,7 @@ class RaggedMeta:
     num_decode: int
     num_prefill: int
     max_query_len: int
+    max_seq_len: int = 0
 
 
 def pack_ragged(
@@ -130,6 +131,7 @@ def pack_ragged(
     *,
     num_decode: int,
     max_query_len: int,
+    max_seq_len: int = 0,
 ) -> RaggedMeta:
     """Expand a per-request plan ``[3, R]`` (table rows, contexts, query lengths)."""
     _require_cuda(plan, block_tables)
@@ -190,6 +192,7 @@ def pack_ragged(
         num_decode=int(num_decode),
         num_prefill=R - int(num_decode),
         max_query_len=int(max_query_len),
+        max_seq_len=int(max_seq_len),
     )
 
 
@@ -437,8 +440,14 @@ def varlen_attention(
     req_list: torch.Tensor | None = None,
     num_requests: int | None = None,
     scale: float | None = None,
+    max_seq_len: int | None = None,
 ) -> torch.Tensor:
-    """Causal varlen attention of ragged query rows over the paged cache."""
+    """Causal varlen attention of ragged query rows over the paged cache.
+
+    ``max_seq_len`` (a host bound on every ``seq_lens`` entry) lets the
+    tensor-core kernel split long key ranges across CTAs; without it each
+    query tile walks all of its keys in one CTA.
+    """
     _require_cuda(query, key_cache, value_cache, block_tables, seq_lens, query_start_loc, table_rows, req_list)
     L, nb, bs, h, d = _cache_geometry(key_cache)
     if query.ndim != 3 or query.shape[2] != d or query.stride(2) != 1 or query.stride(1) != d:
@@ -452,6 +461,9 @@ def varlen_attention(
     if out.stride(0) != query.stride(0):
         raise ValueError("out must share the query row stride")
     device = query.device
+    msl = int(max_seq_len or 0)
+    need = int(lib.nie_varlen_workspace_size(R, int(max_query_len), msl, hq))
+    ws = varlen_workspace(device, need) if need else None
     status = lib.nie_varlen_attention(
         query.data_ptr(),
         out.data_ptr(),
@@ -475,10 +487,26 @@ def varlen_attention(
         _ptr(req_list),
         R,
         int(max_query_len),
+        msl,
         float(d**-0.5 if scale is None else scale),
+        _ptr(ws),
+        0 if ws is None else ws.numel(),
         error_flag(device).data_ptr(),
         _stream(device),
     )
     check(status, "nie_varlen_attention")
-    _count()
+    _count(2 if need else 1)
     return out
+
+
+_varlen_workspaces: dict[int, torch.Tensor] = {}
+
+
+def varlen_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Reusable split-key scratch of the tensor-core varlen kernel on ``device``."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _varlen_workspaces.get(index)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", index))
+        _varlen_workspaces[index] = ws
+    return ws

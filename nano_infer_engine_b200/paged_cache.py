@@ -247,6 +247,7 @@ class PagedKVCache:
             self.allocator.num_blocks,
             num_decode=num_decode,
             max_query_len=max(query_lengths),
+            max_seq_len=max(c + q for c, q in zip(context_lengths, query_lengths)),
         )
 
     # ------------------------------------------------------------ data ops

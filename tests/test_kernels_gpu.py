@@ -256,10 +256,14 @@ def test_varlen_against_oracle(cuda, dtype):
     (31, [0, 130, 4000, 8100, 37], [128, 128, 128, 128, 300]),
     (32, [0], [1000]),
     (33, [15, 16, 17, 255, 256, 257], [2, 16, 127, 129, 3, 64]),
+    (34, [1000, 3000, 16, 0], [128, 50, 1, 200]),
 ])
-def test_tensor_core_varlen_against_oracle(cuda, seed, contexts, qlens):
+@pytest.mark.parametrize("split", [False, True])
+def test_tensor_core_varlen_against_oracle(cuda, seed, contexts, qlens, split):
     """tcgen05 path (bf16, hd 64, bs 16): multi-tile queries, long contexts, ragged
-    ends; stale rows past each sequence end hold NaN and must not leak."""
+    ends; stale rows past each sequence end hold NaN and must not leak.  With
+    ``split`` the key range of long requests is divided over CTAs (1024-key
+    chunks) and merged by the combine kernel."""
     g = torch.Generator().manual_seed(seed)
     bs, hkv, hq = 16, 8, 32
     lens = [c + q for c, q in zip(contexts, qlens)]
@@ -278,7 +282,8 @@ def test_tensor_core_varlen_against_oracle(cuda, seed, contexts, qlens):
         qsl.append(qsl[-1] + n)
     out = ops().varlen_attention(q.to(cuda), dk, dv, 0, _tables_tensor(tables, cuda),
                                  torch.tensor(lens, dtype=torch.int32, device=cuda),
-                                 torch.tensor(qsl, dtype=torch.int64, device=cuda), max(qlens))
+                                 torch.tensor(qsl, dtype=torch.int64, device=cuda), max(qlens),
+                                 max_seq_len=max(lens) if split else None)
     ops().check_device_errors(cuda)
     want = oatt.varlen_attention(q, kc, vc, tables, contexts, qlens, 0)
     got = out.cpu().float()
