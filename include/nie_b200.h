@@ -248,6 +248,46 @@ int nie_varlen_attention(const void* q, void* out, int64_t row_stride, int64_t n
                          int32_t max_seq_len, float scale, void* workspace,
                          size_t workspace_bytes, int32_t* err_flag, void* stream);
 
+/*
+ * Fused elementwise stages of one ragged step.  Each reproduces the rounding
+ * sequence of the torch op chain it replaces (every intermediate that the
+ * reference materialises in the activation dtype is rounded to it).
+ *
+ * nie_add_rmsnorm: sum = x + residual (residual may be NULL), out = weight *
+ * (sum / sqrt(mean(sum^2) + eps)), fp32 inside; sum_out (may be NULL)
+ * receives the rounded sum.  Rows of `hidden` contiguous elements, hidden <=
+ * 4096.  Replaces RmsNorm.forward (nano_infer_engine/layers/rms_norm.py:25-31)
+ * together with the residual adds of layers/decoder.py:55-74.
+ */
+int nie_add_rmsnorm(const void* x, const void* residual, const void* weight,
+                    float eps, int64_t rows, int32_t hidden, int32_t dtype,
+                    void* sum_out, void* out, void* stream);
+
+/*
+ * nie_rope_write_kv: rotary embedding of q and k by per-token sin/cos ([T,
+ * head_dim/2], activation dtype) with the half-split pairing, rotated q to
+ * q_out [T, q_heads, head_dim], rotated k and v stored into the cache slots
+ * (as nie_write_kv).  Replaces the RoPE of layers/rope.py:6-23 applied in
+ * layers/attention.py:551-552 plus the slot write of paged_cache.py:324-382.
+ */
+int nie_rope_write_kv(const void* q, int64_t q_stride, const void* k,
+                      int64_t k_stride, const void* v, int64_t v_stride,
+                      const void* sin, const void* cos, int64_t num_tokens,
+                      int32_t q_heads, int32_t kv_heads, int32_t head_dim,
+                      void* q_out, void* key_cache, void* value_cache,
+                      int32_t dtype, int32_t layer, int64_t num_layers,
+                      int64_t num_blocks, int32_t block_size,
+                      const int64_t* slot_mapping, int32_t* err_flag,
+                      void* stream);
+
+/*
+ * nie_silu_mul: out = silu(gate) * up with silu = x / (1 + exp(-x)) in fp32
+ * and both results rounded like torch (layers/mlp.py:18-22).
+ */
+int nie_silu_mul(const void* gate, int64_t gate_stride, const void* up,
+                 int64_t up_stride, void* out, int64_t rows, int32_t cols,
+                 int32_t dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

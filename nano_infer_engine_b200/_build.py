@@ -24,6 +24,7 @@ SOURCES = (
     "nie_attn_generic.cu",
     "nie_attn_decode.cu",
     "nie_attn_prefill.cu",
+    "nie_fused.cu",
 )
 
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")

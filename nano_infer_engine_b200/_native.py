@@ -67,6 +67,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         + [c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p]
         + [c_void_p, c_void_p, c_int32, c_float, c_void_p, c_void_p],
     ),
+    "nie_add_rmsnorm": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_float, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p],
+    ),
+    "nie_rope_write_kv": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int64]
+        + [c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int64, c_int64]
+        + [c_int32, c_void_p, c_void_p, c_void_p],
+    ),
+    "nie_silu_mul": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
     "nie_varlen_workspace_size": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "nie_varlen_attention": (
         c_int,

@@ -15,7 +15,7 @@ from torch import nn
 
 from .. import ops
 from ..paged_cache import PagedKVCache
-from .rope import Rope, apply_rotary
+from .rope import Rope
 
 
 class GroupedQueryAttention(nn.Module):
@@ -37,6 +37,22 @@ class GroupedQueryAttention(nn.Module):
         self.rope = rope if rope is not None else Rope(self.head_dim)
 
     # ------------------------------------------------------------ kernels
+    def rotate_and_store(
+        self,
+        x: torch.Tensor,
+        meta: ops.RaggedMeta,
+        cache: PagedKVCache,
+        layer_index: int,
+        sin: torch.Tensor,
+        cos: torch.Tensor,
+    ) -> torch.Tensor:
+        """q/k/v projections, RoPE on q and k, k/v into the cache; returns q ``[T, Hq, D]``."""
+        q = self.q_proj(x)
+        k = self.k_proj(x)
+        v = self.v_proj(x)
+        return ops.rope_write_kv(q, k, v, sin, cos, cache.keys, cache.values, layer_index, meta.slot_mapping,
+                                 self.q_head_num)
+
     def attend(
         self,
         x: torch.Tensor,
@@ -46,14 +62,14 @@ class GroupedQueryAttention(nn.Module):
         sin: torch.Tensor,
         cos: torch.Tensor,
     ) -> torch.Tensor:
-        """One layer of ragged attention for flattened ``x [T, hidden]``."""
+        """One layer of ragged attention for flattened ``x [T, hidden]``.
+
+        Projections on torch, then one fused kernel rotates q/k (the
+        reference's RoPE rounding) and writes k/v into the cache slots, then
+        the decode and varlen attention kernels, then o_proj.
+        """
         T = x.shape[0]
-        q = self.q_proj(x).view(T, self.q_head_num, self.head_dim)
-        k = self.k_proj(x).view(T, self.kv_head_num, self.head_dim)
-        v = self.v_proj(x).view(T, self.kv_head_num, self.head_dim)
-        q = apply_rotary(q, sin, cos)
-        k = apply_rotary(k, sin, cos)
-        ops.write_kv(k, v, cache.keys, cache.values, layer_index, meta.slot_mapping)
+        q = self.rotate_and_store(x, meta, cache, layer_index, sin, cos)
         out = torch.empty_like(q)
         if meta.num_decode:
             ops.paged_decode(

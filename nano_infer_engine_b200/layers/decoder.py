@@ -27,16 +27,25 @@ class Llama3Decoder(nn.Module):
 
     def step(
         self,
-        x: torch.Tensor,
+        normed: torch.Tensor,
+        residual: torch.Tensor,
         meta: ops.RaggedMeta,
         cache: PagedKVCache,
         layer_index: int,
         sin: torch.Tensor,
         cos: torch.Tensor,
-    ) -> torch.Tensor:
-        """Residual block on flattened tokens with precomputed metadata."""
-        h = self.attn.attend(self.pre_norm(x), meta, cache, layer_index, sin, cos) + x
-        return self.ffn(self.post_norm(h)) + h
+    ) -> tuple[torch.Tensor, torch.Tensor]:
+        """One block on flattened tokens whose pre-norm is already applied.
+
+        Returns ``(mlp_out, h)`` with ``h = attn_out + residual``; the caller
+        adds the two inside the next fused add + RMSNorm, which is the
+        reference order (``h = attn + x``, ``out = mlp(norm(h)) + h``).
+        """
+        attn = self.attn.attend(normed, meta, cache, layer_index, sin, cos)
+        h, normed2 = ops.add_rmsnorm(attn, residual, self.post_norm.weight, self.post_norm.eps)
+        gate = self.ffn.gate_proj(normed2)
+        up = self.ffn.up_proj(normed2)
+        return self.ffn.down_proj(ops.silu_mul(gate, up)), h
 
     def forward(self, x, k_cache=None, v_cache=None, cache_position=0, attention_mask=None, position_ids=None, *,
                 paged_cache=None, layer_index=None, sequence_id="default", sequence_ids=None):

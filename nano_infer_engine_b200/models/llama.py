@@ -224,15 +224,30 @@ class Llama3_2(nn.Module):
         rope_positions: torch.Tensor | None = None,
         logit_rows: torch.Tensor | None = None,
     ) -> torch.Tensor:
-        """Embed -> decoders -> norm -> lm_head over flattened tokens."""
+        """Embed -> decoders -> norm -> lm_head over flattened tokens.
+
+        Residual adds are folded into the next RMSNorm (fused kernel), so a
+        layer is: add+norm, q/k/v GEMMs, RoPE+KV write, attention, o_proj,
+        add+norm, gate/up GEMMs, SiLU*up, down GEMM.
+        """
         x = self.embed(input_ids)
         positions = meta.positions if rope_positions is None else rope_positions
         sin, cos = self.rope.sin_cos(positions, x.dtype)
+        first = self.decoders[0].pre_norm
+        residual = x
+        _, normed = ops.add_rmsnorm(x, None, first.weight, first.eps)
+        last = len(self.decoders) - 1
         for layer_index, decoder in enumerate(self.decoders):
-            x = decoder.step(x, meta, cache, layer_index, sin, cos)
-        if logit_rows is not None:
-            x = x.index_select(0, logit_rows)
-        return self.lm_head(self.final_rms(x))
+            mlp_out, h = decoder.step(normed, residual, meta, cache, layer_index, sin, cos)
+            if layer_index < last:
+                nxt = self.decoders[layer_index + 1].pre_norm
+                residual, normed = ops.add_rmsnorm(mlp_out, h, nxt.weight, nxt.eps)
+            else:
+                if logit_rows is not None:
+                    mlp_out = mlp_out.index_select(0, logit_rows)
+                    h = h.index_select(0, logit_rows)
+                _, normed = ops.add_rmsnorm(mlp_out, h, self.final_rms.weight, self.final_rms.eps, want_sum=False)
+        return self.lm_head(normed)
 
     def _decode_step(
         self,

@@ -510,3 +510,117 @@ def varlen_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", index))
         _varlen_workspaces[index] = ws
     return ws
+
+
+# ----------------------------------------------------- fused elementwise
+def add_rmsnorm(
+    x: torch.Tensor,
+    residual: torch.Tensor | None,
+    weight: torch.Tensor,
+    eps: float,
+    *,
+    want_sum: bool = True,
+) -> tuple[torch.Tensor | None, torch.Tensor]:
+    """``(x + residual, rmsnorm(x + residual) * weight)`` over the last dim, torch rounding."""
+    _require_cuda(x, residual, weight)
+    hidden = x.shape[-1]
+    x = x.contiguous()
+    if residual is not None:
+        residual = residual.contiguous()
+        if residual.shape != x.shape or residual.dtype != x.dtype:
+            raise ValueError("residual must match x")
+    rows = x.numel() // hidden
+    out = torch.empty_like(x)
+    total = torch.empty_like(x) if (want_sum and residual is not None) else None
+    status = lib.nie_add_rmsnorm(
+        x.data_ptr(),
+        _ptr(residual),
+        weight.data_ptr(),
+        float(eps),
+        rows,
+        hidden,
+        dtype_code(x.dtype),
+        _ptr(total),
+        out.data_ptr(),
+        _stream(x.device),
+    )
+    check(status, "nie_add_rmsnorm")
+    _count()
+    return (total if residual is not None else x), out
+
+
+def rope_write_kv(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    sin: torch.Tensor,
+    cos: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    layer: int,
+    slot_mapping: torch.Tensor,
+    q_heads: int,
+) -> torch.Tensor:
+    """Rotate q/k (rows ``[T, heads*D]`` with a row stride) and write k/v to the cache slots.
+
+    Returns the rotated queries as ``[T, q_heads, D]``.
+    """
+    _require_cuda(q, k, v, sin, cos, key_cache, value_cache, slot_mapping)
+    L, nb, bs, h, d = _cache_geometry(key_cache)
+    T = q.shape[0]
+    for t, width in ((q, q_heads * d), (k, h * d), (v, h * d)):
+        if t.ndim != 2 or t.shape[1] != width or t.stride(1) != 1:
+            raise ValueError("q/k/v must be [T, heads*head_dim] with unit inner stride")
+    if sin.shape != (T, d // 2) or not sin.is_contiguous() or not cos.is_contiguous():
+        raise ValueError("sin/cos must be contiguous [T, head_dim/2]")
+    q_out = torch.empty((T, q_heads, d), dtype=q.dtype, device=q.device)
+    status = lib.nie_rope_write_kv(
+        q.data_ptr(),
+        q.stride(0),
+        k.data_ptr(),
+        k.stride(0),
+        v.data_ptr(),
+        v.stride(0),
+        sin.data_ptr(),
+        cos.data_ptr(),
+        T,
+        q_heads,
+        h,
+        d,
+        q_out.data_ptr(),
+        key_cache.data_ptr(),
+        value_cache.data_ptr(),
+        dtype_code(q.dtype),
+        layer,
+        L,
+        nb,
+        bs,
+        slot_mapping.data_ptr(),
+        error_flag(q.device).data_ptr(),
+        _stream(q.device),
+    )
+    check(status, "nie_rope_write_kv")
+    _count()
+    return q_out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """``silu(gate) * up`` with torch's rounding, rows ``[T, inner]`` (row strides allowed)."""
+    _require_cuda(gate, up)
+    if gate.shape != up.shape or gate.ndim != 2 or gate.stride(1) != 1 or up.stride(1) != 1:
+        raise ValueError("gate/up must be matching [T, inner] with unit inner stride")
+    out = torch.empty(gate.shape, dtype=gate.dtype, device=gate.device)
+    status = lib.nie_silu_mul(
+        gate.data_ptr(),
+        gate.stride(0),
+        up.data_ptr(),
+        up.stride(0),
+        out.data_ptr(),
+        gate.shape[0],
+        gate.shape[1],
+        dtype_code(gate.dtype),
+        _stream(gate.device),
+    )
+    check(status, "nie_silu_mul")
+    _count()
+    return out

@@ -333,3 +333,51 @@ def test_mixed_step_config4_shape(cuda):
     assert torch.equal(dk.cpu(), kc2) and torch.equal(dv.cpu(), vc2)
     want = oatt.varlen_attention(q, kc2, vc2, tables, contexts, qlens, 0)
     torch.testing.assert_close(out.cpu().float(), want.float(), atol=2e-2, rtol=0)
+
+
+# ------------------------------------------------ fused elementwise stages
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_rope_write_matches_torch_ops(cuda, dtype):
+    """RoPE + slot write equals the torch op chain (reference layers/rope.py:6-23) bit for bit."""
+    from nano_infer_engine_b200.layers.rope import RopeScale, apply_rotary
+
+    g = torch.Generator().manual_seed(50)
+    T, hq, hkv, d, bs, nb = 37, 32, 8, 64, 16, 40
+    q = torch.randn(T, hq * d, generator=g).to(dtype).to(cuda)
+    k = torch.randn(T, hkv * d, generator=g).to(dtype).to(cuda)
+    v = torch.randn(T, hkv * d, generator=g).to(dtype).to(cuda)
+    pos = torch.randint(0, 30000, (T,), generator=g).to(cuda)
+    sin, cos = RopeScale(d).sin_cos(pos, dtype)
+    kc = torch.zeros(2, nb, bs, hkv, d, dtype=dtype, device=cuda)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(nb * bs, generator=g)[:T].to(cuda)
+    qr = ops().rope_write_kv(q, k, v, sin, cos, kc, vc, 1, slots, hq)
+    want_q = apply_rotary(q.view(T, hq, d), sin, cos)
+    want_k = apply_rotary(k.view(T, hkv, d), sin, cos)
+    assert torch.equal(qr, want_q)
+    flat_k = kc[1].view(-1, hkv, d)
+    flat_v = vc[1].view(-1, hkv, d)
+    assert torch.equal(flat_k[slots], want_k)
+    assert torch.equal(flat_v[slots], v.view(T, hkv, d))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_silu_mul_and_add_rmsnorm_match_torch_ops(cuda, dtype):
+    from nano_infer_engine_b200.layers.rms_norm import RmsNorm
+
+    g = torch.Generator().manual_seed(51)
+    gate = torch.randn(19, 8192, generator=g).to(dtype).to(cuda)
+    up = torch.randn(19, 8192, generator=g).to(dtype).to(cuda)
+    assert torch.equal(ops().silu_mul(gate, up), torch.nn.functional.silu(gate) * up)
+    x = torch.randn(19, 2048, generator=g).to(dtype).to(cuda)
+    r = torch.randn(19, 2048, generator=g).to(dtype).to(cuda)
+    norm = RmsNorm(2048, 1e-5).to(cuda)
+    with torch.no_grad():
+        norm.weight.copy_(torch.rand(2048, generator=g) + 0.5)
+    norm = norm.to(dtype)
+    total, out = ops().add_rmsnorm(x, r, norm.weight, 1e-5)
+    assert torch.equal(total, x + r)
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    torch.testing.assert_close(out.float(), norm(x + r).float(), atol=tol, rtol=tol)
+    _, plain = ops().add_rmsnorm(x, None, norm.weight, 1e-5)
+    torch.testing.assert_close(plain.float(), norm(x).float(), atol=tol, rtol=tol)
