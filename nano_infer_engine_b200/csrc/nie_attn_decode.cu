@@ -389,8 +389,10 @@ __global__ void __launch_bounds__(512, 1)
 }
 
 // Merge the partials of requests whose blocks were split across CTAs.
-__global__ void __launch_bounds__(256) decode_combine_kernel(DecodeArgs a) {
-  const int i = blockIdx.x;
+// grid = (requests, q_heads), one thread per head-dim element: every load of
+// a split is independent of the others (the chain is only the final sums).
+__global__ void __launch_bounds__(kDecHD) decode_combine_kernel(DecodeArgs a) {
+  const int i = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int R = a.num_req;
   const int32_t* cum = a.cum_out;
   const int W = cum[R + 1];
@@ -401,19 +403,20 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeArgs a) {
   const int req = a.req_list ? a.req_list[i] : i;
   const int64_t qrow = a.q_rows ? a.q_rows[req] : (int64_t)req;
   const int64_t stride = (int64_t)a.hq * (kDecHD + 2);
-  for (int idx = threadIdx.x; idx < a.hq * kDecHD; idx += blockDim.x) {
-    const int h = idx / kDecHD, d = idx % kDecHD;
-    float M = -INFINITY;
-    for (int c = c0; c <= c1; ++c) M = fmaxf(M, a.partials[(int64_t)(c + i) * stride + h]);
-    float L = 0.f, O = 0.f;
-    for (int c = c0; c <= c1; ++c) {
-      const float* ps = a.partials + (int64_t)(c + i) * stride;
-      const float w = fast_exp2(ps[h] - M);
-      L += ps[a.hq + h] * w;
-      O += ps[2 * a.hq + h * kDecHD + d] * w;
-    }
-    a.out[qrow * a.out_stride + (int64_t)h * kDecHD + d] = __float2bfloat16_rn(O / L);
+  const float* base = a.partials + (int64_t)(c0 + i) * stride;
+  const int n = c1 - c0 + 1;
+  float M = -INFINITY;
+#pragma unroll 4
+  for (int c = 0; c < n; ++c) M = fmaxf(M, base[c * stride + h]);
+  float L = 0.f, O = 0.f;
+#pragma unroll 4
+  for (int c = 0; c < n; ++c) {
+    const float* ps = base + c * stride;
+    const float w = fast_exp2(ps[h] - M);
+    L += ps[a.hq + h] * w;
+    O += ps[2 * a.hq + h * kDecHD + d] * w;
   }
+  a.out[qrow * a.out_stride + (int64_t)h * kDecHD + d] = __float2bfloat16_rn(O / L);
 }
 
 static size_t ws_header_bytes(int R) { return (((size_t)(R + 2) * sizeof(int32_t)) + 255) & ~size_t(255); }
@@ -544,7 +547,7 @@ extern "C" int nie_paged_decode(const void* q, int64_t q_row_stride, void* out, 
   decode_tma_kernel<kDecStages><<<grid, kv_heads * 32, smem, s>>>(kmap, vmap, da);
   rc = check_launch("decode_tma_kernel");
   if (rc != NIE_OK) return rc;
-  decode_combine_kernel<<<num_requests, 256, 0, s>>>(da);
+  decode_combine_kernel<<<dim3((unsigned)num_requests, (unsigned)q_heads), kDecHD, 0, s>>>(da);
   return check_launch("decode_combine_kernel");
 }
 

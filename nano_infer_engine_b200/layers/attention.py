@@ -18,6 +18,42 @@ from ..paged_cache import PagedKVCache
 from .rope import Rope
 
 
+def fused_weight(module: nn.Module, names: tuple[str, ...], attr: str) -> torch.Tensor | None:
+    """The concatenated weight of ``names`` if their parameters are still views of it."""
+    buf = module.__dict__.get(attr)
+    if buf is None:
+        return None
+    at = buf.data_ptr()
+    step = buf.element_size()
+    for name in names:
+        w = getattr(module, name).weight
+        if w.data_ptr() != at or w.dtype != buf.dtype:
+            return None
+        at += w.numel() * step
+    return buf
+
+
+def fuse_linears(module: nn.Module, names: tuple[str, ...], attr: str) -> bool:
+    """Concatenate the weights of bias-free Linear children ``names`` (rows) into one buffer.
+
+    The children's ``weight`` parameters are rebound as views of the buffer,
+    so ``load_state_dict`` keeps writing through to it.  Returns True if the
+    buffer was built now.
+    """
+    if fused_weight(module, names, attr) is not None:
+        return False
+    linears = [getattr(module, n) for n in names]
+    with torch.inference_mode(False), torch.no_grad():
+        buf = torch.cat([lin.weight.detach() for lin in linears], dim=0)
+        start = 0
+        for lin in linears:
+            rows = lin.weight.shape[0]
+            lin.weight = nn.Parameter(buf[start : start + rows], requires_grad=lin.weight.requires_grad)
+            start += rows
+    module.__dict__[attr] = buf
+    return True
+
+
 class GroupedQueryAttention(nn.Module):
     """Reference attention.py:121-145 parameters (q/k/v/o projections, shared rope)."""
 
@@ -37,6 +73,14 @@ class GroupedQueryAttention(nn.Module):
         self.rope = rope if rope is not None else Rope(self.head_dim)
 
     # ------------------------------------------------------------ kernels
+    def fuse_projections(self) -> bool:
+        """Store q/k/v weights in one buffer (the parameters become views of it).
+
+        One GEMM then produces q, k and v.  Returns True when the buffer was
+        (re)built, e.g. after ``.to()`` replaced the parameters.
+        """
+        return fuse_linears(self, ("q_proj", "k_proj", "v_proj"), "_qkv")
+
     def rotate_and_store(
         self,
         x: torch.Tensor,
@@ -47,9 +91,16 @@ class GroupedQueryAttention(nn.Module):
         cos: torch.Tensor,
     ) -> torch.Tensor:
         """q/k/v projections, RoPE on q and k, k/v into the cache; returns q ``[T, Hq, D]``."""
-        q = self.q_proj(x)
-        k = self.k_proj(x)
-        v = self.v_proj(x)
+        fused = fused_weight(self, ("q_proj", "k_proj", "v_proj"), "_qkv")
+        if fused is not None:
+            qkv = torch.nn.functional.linear(x, fused)
+            nq = self.q_head_num * self.head_dim
+            nkv = self.kv_head_num * self.head_dim
+            q, k, v = qkv[:, :nq], qkv[:, nq : nq + nkv], qkv[:, nq + nkv :]
+        else:
+            q = self.q_proj(x)
+            k = self.k_proj(x)
+            v = self.v_proj(x)
         return ops.rope_write_kv(q, k, v, sin, cos, cache.keys, cache.values, layer_index, meta.slot_mapping,
                                  self.q_head_num)
 

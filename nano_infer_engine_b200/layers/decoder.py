@@ -7,7 +7,7 @@ from torch import nn
 
 from .. import ops
 from ..paged_cache import PagedKVCache
-from .attention import GroupedQueryAttention
+from .attention import GroupedQueryAttention, fuse_linears, fused_weight
 from .mlp import SwiGLUMLP
 from .rms_norm import RmsNorm
 
@@ -43,9 +43,20 @@ class Llama3Decoder(nn.Module):
         """
         attn = self.attn.attend(normed, meta, cache, layer_index, sin, cos)
         h, normed2 = ops.add_rmsnorm(attn, residual, self.post_norm.weight, self.post_norm.eps)
-        gate = self.ffn.gate_proj(normed2)
-        up = self.ffn.up_proj(normed2)
+        fused = fused_weight(self.ffn, ("gate_proj", "up_proj"), "_gate_up")
+        if fused is not None:
+            gate_up = torch.nn.functional.linear(normed2, fused)
+            inner = self.ffn.inner_size
+            gate, up = gate_up[:, :inner], gate_up[:, inner:]
+        else:
+            gate = self.ffn.gate_proj(normed2)
+            up = self.ffn.up_proj(normed2)
         return self.ffn.down_proj(ops.silu_mul(gate, up)), h
+
+    def fuse_projections(self) -> bool:
+        """Single-buffer q/k/v and gate/up weights (see ``fuse_linears``)."""
+        changed = self.attn.fuse_projections()
+        return fuse_linears(self.ffn, ("gate_proj", "up_proj"), "_gate_up") or changed
 
     def forward(self, x, k_cache=None, v_cache=None, cache_position=0, attention_mask=None, position_ids=None, *,
                 paged_cache=None, layer_index=None, sequence_id="default", sequence_ids=None):

@@ -160,6 +160,7 @@ class _DecodeGraph:
         self.ids = torch.zeros(batch, dtype=torch.long, device=dev)
         self.plan = torch.zeros((3, batch), dtype=torch.int32, device=dev)
         self.table = cache.device_block_tables()
+        self.generation = model._ensure_fused()
         self.graph = torch.cuda.CUDAGraph()
         launches = ops.LAUNCHES
         with torch.cuda.graph(self.graph):
@@ -230,6 +231,7 @@ class Llama3_2(nn.Module):
         layer is: add+norm, q/k/v GEMMs, RoPE+KV write, attention, o_proj,
         add+norm, gate/up GEMMs, SiLU*up, down GEMM.
         """
+        self._ensure_fused()
         x = self.embed(input_ids)
         positions = meta.positions if rope_positions is None else rope_positions
         sin, cos = self.rope.sin_cos(positions, x.dtype)
@@ -249,6 +251,24 @@ class Llama3_2(nn.Module):
                 _, normed = ops.add_rmsnorm(mlp_out, h, self.final_rms.weight, self.final_rms.eps, want_sum=False)
         return self.lm_head(normed)
 
+    def _ensure_fused(self) -> int:
+        """Keep q/k/v and gate/up weights in single buffers; returns their generation.
+
+        A cheap signature (first and last layer pointers) detects parameters
+        replaced wholesale, e.g. by ``.to()``; the buffers are then rebuilt and
+        the generation bumps, which retires captured graphs.
+        """
+        first, last = self.decoders[0], self.decoders[-1]
+        sig = (first.attn.q_proj.weight.data_ptr(), last.ffn.up_proj.weight.data_ptr())
+        if self.__dict__.get("_fused_sig") != sig:
+            changed = False
+            for decoder in self.decoders:
+                changed = decoder.fuse_projections() or changed
+            if changed:
+                self.__dict__["_weights_gen"] = self.__dict__.get("_weights_gen", 0) + 1
+            self.__dict__["_fused_sig"] = (first.attn.q_proj.weight.data_ptr(), last.ffn.up_proj.weight.data_ptr())
+        return self.__dict__.get("_weights_gen", 0)
+
     def _decode_step(
         self,
         input_ids: torch.Tensor,
@@ -266,9 +286,10 @@ class Llama3_2(nn.Module):
         table = cache.device_block_tables()
         graphs = cache.__dict__.setdefault("_decode_graphs", {})
         key = (id(self), batch)
+        generation = self._ensure_fused()
         graph = graphs.get(key)
-        if graph is not None and graph.table is not table:
-            graph = None  # the block-table tensor was reallocated
+        if graph is not None and (graph.table is not table or graph.generation != generation):
+            graph = None  # the block-table tensor or the weight buffers were reallocated
         if graph is None:
             meta = cache.pack(sequence_ids, context_lengths, (1,) * batch)
             logits = self.run_ragged(input_ids, meta, cache)
