@@ -142,6 +142,21 @@ int nie_copy_blocks(const void* src_keys, const void* src_values,
 int nie_enable_peer_access(int device, int peer_device);
 
 /*
+ * CUDA IPC for prefill/decode processes (one process per GPU).  The
+ * reference moves KV between devices inside one process
+ * (paged_cache.py:288-294); with a process per GPU the decode process maps
+ * the prefill process's pool and nie_copy_blocks pulls blocks over NVLink.
+ * nie_ipc_export writes the 64-byte handle of the allocation that contains
+ * `ptr` and ptr's offset in it; nie_ipc_import (in another process, on the
+ * current device) maps it with lazy peer access and returns the pointer and
+ * the mapping base, which nie_ipc_close releases.
+ */
+int nie_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+int nie_ipc_import(const void* handle, uint64_t offset, void** ptr_out,
+                   void** base_out);
+int nie_ipc_close(void* base);
+
+/*
  * (c) Paged decode attention: one query token per request.
  * Replaces batched_paged_attention_reference
  * (nano_infer_engine/layers/paged_attention.py:117-176, per-sequence body

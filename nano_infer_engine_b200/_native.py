@@ -53,6 +53,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         + [c_int64, c_int32, c_int32, c_int64, c_int32, c_int32, c_int32, c_void_p, c_void_p],
     ),
     "nie_enable_peer_access": (c_int, [c_int, c_int]),
+    "nie_ipc_export": (c_int, [c_void_p, c_void_p, ctypes.POINTER(ctypes.c_uint64)]),
+    "nie_ipc_import": (c_int, [c_void_p, ctypes.c_uint64, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p)]),
+    "nie_ipc_close": (c_int, [c_void_p]),
     "nie_paged_decode_workspace_size": (c_size_t, [c_int, c_int32, c_int32, c_int32]),
     "nie_paged_decode": (
         c_int,

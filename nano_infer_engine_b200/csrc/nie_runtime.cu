@@ -90,6 +90,54 @@ extern "C" const char* nie_last_error(void) { return nie::g_last_error; }
 
 extern "C" int nie_device_sm_count(int device) { return nie::sm_count(device); }
 
+namespace nie {
+static PFN_cuMemGetAddressRange_v3020 g_addr_range = nullptr;
+}
+
+extern "C" int nie_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out) {
+  NIE_REQUIRE(ptr && handle_out && offset_out, "null pointer argument");
+  {
+    std::lock_guard<std::mutex> lk(nie::g_mu);
+    if (nie::g_addr_range == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      cudaError_t e = cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 3020, cudaEnableDefault, &q);
+      if (e != cudaSuccess || fn == nullptr || q != cudaDriverEntryPointSuccess)
+        return nie::fail(NIE_ERR_CUDA, "cannot resolve cuMemGetAddressRange");
+      nie::g_addr_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+    }
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = nie::g_addr_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return nie::fail(NIE_ERR_CUDA, "cuMemGetAddressRange failed (CUresult %d)", (int)r);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return nie::fail(NIE_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = (uint64_t)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return NIE_OK;
+}
+
+extern "C" int nie_ipc_import(const void* handle, uint64_t offset, void** ptr_out, void** base_out) {
+  NIE_REQUIRE(handle && ptr_out && base_out, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return nie::fail(NIE_ERR_CUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  *base_out = base;
+  *ptr_out = static_cast<char*>(base) + offset;
+  return NIE_OK;
+}
+
+extern "C" int nie_ipc_close(void* base) {
+  NIE_REQUIRE(base, "null pointer argument");
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return nie::fail(NIE_ERR_CUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+  return NIE_OK;
+}
+
 extern "C" int nie_enable_peer_access(int device, int peer_device) {
   if (device == peer_device) return NIE_OK;
   int can = 0;

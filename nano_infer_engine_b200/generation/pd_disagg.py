@@ -1,0 +1,282 @@
+"""Prefill/decode disaggregation with one process per GPU.
+
+The reference runs P/D inside one process that owns two devices
+(generation/pd_scheduler.py:136-181, service/runtime.py:277-358): prefill,
+``export_sequence`` on the prefill device, ``import_sequence`` with a
+per-block cross-device ``copy_`` on the decode device, then
+``add_prefilled_request``.  Here each GPU has its own process:
+
+* a **pair** is (prefill rank, decode rank); a deterministic router assigns
+  requests to pairs (least outstanding work);
+* at set-up the prefill rank exports its KV pool with CUDA IPC and the
+  decode rank maps it on its own device (``ops.ipc_import``);
+* the prefill rank prefills batches of prompts as one ragged call, reads the
+  greedy first tokens, and sends a HANDOFF message per request with its
+  length, first token and physical block ids;
+* the decode rank allocates blocks in its pool, **pulls** the blocks over
+  NVLink with the block-copy kernel (zeroed tail as in the reference export),
+  admits the request into its own continuous-batching scheduler and, once the
+  copy has completed, sends an ACK so the prefill rank can free its blocks.
+
+Messages are int64 records in the process group's key-value store, polled
+without blocking.  The GPU-specific steps (prefill, block import) are
+injectable so the protocol runs with gloo on CPU in tests.
+"""
+
+from __future__ import annotations
+
+import time
+from collections import deque
+from collections.abc import Callable
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..paged_cache import PagedKVCache
+from .config import GenerationConfig
+from .paged_prefill import paged_prefill_chunks
+from .request import PagedRequest
+from .scheduler import ContinuousBatchingScheduler
+
+HANDOFF = 1
+ACK = 2
+DONE = 3
+HEADER_WORDS = 8
+
+
+def assign_pairs(work: list[int], num_pairs: int) -> list[list[int]]:
+    """Request indices per pair: each request (in arrival order) goes to the pair
+    with the least outstanding work so far (ties: lowest pair index)."""
+    load = [0] * num_pairs
+    out: list[list[int]] = [[] for _ in range(num_pairs)]
+    for index, w in enumerate(work):
+        pair = min(range(num_pairs), key=lambda p: (load[p], p))
+        out[pair].append(index)
+        load[pair] += w
+    return out
+
+
+class PairChannel:
+    """Ordered int64 messages between the two ranks of a pair, polled without blocking.
+
+    Messages travel through the process group's key-value store (any c10d
+    ``Store``): the n-th message from rank a to rank b is key ``pd/a->b/n``,
+    deleted by the receiver once read.  ``Store.check`` does not block, so
+    both loops keep stepping their models while no message is waiting.
+    """
+
+    def __init__(self, store, me: int, peer: int, words: int) -> None:
+        self.store = store
+        self.words = words
+        self._out = f"pd/{me}->{peer}/"
+        self._in = f"pd/{peer}->{me}/"
+        self._sent = 0
+        self._received = 0
+
+    def send(self, values: list[int]) -> None:
+        if len(values) > self.words:
+            raise ValueError("message longer than the channel's fixed size")
+        msg = np.zeros(self.words, dtype=np.int64)
+        msg[: len(values)] = values
+        self.store.set(self._out + str(self._sent), msg.tobytes())
+        self._sent += 1
+
+    def poll(self) -> list[list[int]]:
+        out = []
+        while True:
+            key = self._in + str(self._received)
+            if not self.store.check([key]):
+                return out
+            out.append(np.frombuffer(self.store.get(key), dtype=np.int64).tolist())
+            self.store.delete_key(key)
+            self._received += 1
+
+    def close(self) -> None:
+        """Messages are delivered when ``send`` returns; nothing is left in flight."""
+
+
+@dataclass
+class RemotePool:
+    """The prefill rank's KV pool as mapped into the decode process."""
+
+    keys_ptr: int
+    values_ptr: int
+    num_blocks: int
+    bases: tuple[int, int]
+    device: torch.device
+
+    def close(self) -> None:
+        for base in self.bases:
+            ops.ipc_close(base, self.device)
+
+
+def export_pool(cache: PagedKVCache) -> dict:
+    kh, ko = ops.ipc_export(cache.keys)
+    vh, vo = ops.ipc_export(cache.values)
+    return {
+        "keys": (kh, ko),
+        "values": (vh, vo),
+        "shape": tuple(cache.keys.shape),
+        "dtype": str(cache.keys.dtype),
+    }
+
+
+def import_pool(exported: dict, cache: PagedKVCache) -> RemotePool:
+    if tuple(exported["shape"][0:1] + exported["shape"][2:]) != (cache.num_layers, cache.block_size,
+                                                                  cache.kv_head_num, cache.head_dim):
+        raise ValueError("prefill and decode pools must share layers, block size and head geometry")
+    if exported["dtype"] != str(cache.keys.dtype):
+        raise ValueError("prefill and decode pools must share a dtype")
+    kp, kb = ops.ipc_import(*exported["keys"], cache.device)
+    vp, vb = ops.ipc_import(*exported["values"], cache.device)
+    return RemotePool(kp, vp, exported["shape"][1], (kb, vb), cache.device)
+
+
+def gpu_import(remote: RemotePool):
+    """Block import for the decode worker: allocate, pull over NVLink, advance."""
+
+    def _import(cache: PagedKVCache, sequence_id: str, length: int, src_blocks: list[int]):
+        n = -(-length // cache.block_size)
+        cache.ensure_capacity(sequence_id, length)
+        dst = cache.get_block_table(sequence_id)[:n]
+        dev = cache.device
+        src_t = torch.tensor(src_blocks[:n], dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        dst_t = torch.tensor(dst, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        ops.copy_blocks_from_pointers(remote.keys_ptr, remote.values_ptr, remote.num_blocks, src_t, cache.keys,
+                                      cache.values, dst_t, n, length % cache.block_size)
+        cache.advance(sequence_id, length)
+        event = torch.cuda.Event()
+        event.record()
+        return event
+
+    return _import
+
+
+@dataclass
+class PrefillStats:
+    requests: int = 0
+    tokens: int = 0
+    batches: int = 0
+
+
+def run_prefill(
+    model,
+    cache: PagedKVCache,
+    channel: PairChannel,
+    requests: list[tuple[int, torch.Tensor]],
+    *,
+    token_budget: int = 8192,
+    arrival: list[float] | None = None,
+    clock: Callable[[], float] = time.perf_counter,
+    idle_sleep: float = 0.0,
+) -> PrefillStats:
+    """Prefill ``(index, prompt[1, n])`` requests in order and hand them to the decode peer.
+
+    Batches are formed from arrived requests up to ``token_budget`` prompt
+    tokens and the free blocks of ``cache``; a request's blocks are held
+    until the decode peer acknowledges its copy.  ``arrival`` (seconds from
+    the start, same order as ``requests``) gates admission for open-loop runs.
+    """
+    stats = PrefillStats()
+    pending = deque(range(len(requests)))
+    held: dict[int, str] = {}
+    bs = cache.block_size
+    start = clock()
+    while pending or held:
+        for msg in channel.poll():
+            if msg[0] == ACK:
+                cache.release(held.pop(msg[1]))
+        batch: list[int] = []
+        tokens = 0
+        blocks = 0
+        now = clock() - start
+        while pending:
+            k = pending[0]
+            if arrival is not None and arrival[k] > now:
+                break
+            n = requests[k][1].shape[1]
+            need = -(-n // bs)
+            if batch and (tokens + n > token_budget or blocks + need > cache.allocator.free_block_count):
+                break
+            if not batch and need > cache.allocator.free_block_count:
+                break
+            batch.append(pending.popleft())
+            tokens += n
+            blocks += need
+        if not batch:
+            if idle_sleep:
+                time.sleep(idle_sleep)
+            continue
+        ids = tuple(f"pd-{requests[k][0]}" for k in batch)
+        chunks = tuple(requests[k][1] for k in batch)
+        with torch.inference_mode():
+            logits = paged_prefill_chunks(model, chunks, cache, ids)
+            first = logits.argmax(dim=-1).tolist()  # also waits for the KV writes
+        for k, sid, tok in zip(batch, ids, first):
+            index, prompt = requests[k]
+            table = cache.get_block_table(sid)
+            channel.send([HANDOFF, index, prompt.shape[1], int(tok), len(table), 0, 0, 0, *table])
+            held[index] = sid
+        stats.requests += len(batch)
+        stats.tokens += tokens
+        stats.batches += 1
+    channel.send([DONE, stats.requests])
+    channel.close()
+    return stats
+
+
+def run_decode(
+    model,
+    cache: PagedKVCache,
+    channel: PairChannel,
+    prompt_of: Callable[[int], torch.Tensor],
+    config: GenerationConfig,
+    max_batch_size: int,
+    import_fn: Callable,
+    vocab_size: int,
+    *,
+    idle_sleep: float = 0.0,
+) -> list[PagedRequest]:
+    """Receive hand-offs, import their KV, and decode them with continuous batching."""
+    sched = ContinuousBatchingScheduler(model, config, cache, max_batch_size)
+    ready: deque[tuple[PagedRequest, torch.Tensor]] = deque()
+    copies: deque[tuple[object, int]] = deque()
+    requests: list[PagedRequest] = []
+    done = False
+    bs = cache.block_size
+    dtype = cache.keys.dtype
+    while True:
+        for msg in channel.poll():
+            if msg[0] == HANDOFF:
+                index, length, token, nblk = msg[1], msg[2], msg[3], msg[4]
+                sid = f"pd-{index}"
+                event = import_fn(cache, sid, length, msg[HEADER_WORDS : HEADER_WORDS + nblk])
+                prompt = prompt_of(index)
+                required = (length + config.max_new_tokens - 1 + bs - 1) // bs
+                request = PagedRequest(sequence_id=sid, prompt=prompt, required_blocks=required)
+                logits = torch.zeros(vocab_size, dtype=dtype, device=cache.device)
+                logits[token] = 1
+                ready.append((request, logits))
+                copies.append((event, index))
+            elif msg[0] == DONE:
+                done = True
+        while copies and (copies[0][0] is None or copies[0][0].query()):
+            channel.send([ACK, copies.popleft()[1]])
+        while (
+            ready
+            and sched.active_count < max_batch_size
+            and sched.reserved_blocks + ready[0][0].required_blocks <= sched.block_budget
+        ):
+            request, logits = ready.popleft()
+            sched.add_prefilled_request(request, logits)
+            requests.append(request)
+        if sched.has_work:
+            sched.step()
+        elif done and not ready and not copies:
+            break
+        elif idle_sleep:
+            time.sleep(idle_sleep)
+    channel.close()
+    return requests

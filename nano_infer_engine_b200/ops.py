@@ -8,6 +8,7 @@ is no CPU implementation.  Shapes follow the reference's cache layout
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -331,6 +332,70 @@ def copy_blocks(
         )
     check(status, "nie_copy_blocks")
     _count()
+
+
+def copy_blocks_from_pointers(
+    src_keys_ptr: int,
+    src_values_ptr: int,
+    src_num_blocks: int,
+    src_blocks: torch.Tensor,
+    dst_keys: torch.Tensor,
+    dst_values: torch.Tensor,
+    dst_blocks: torch.Tensor,
+    num_copy_blocks: int,
+    tail_valid_tokens: int,
+) -> None:
+    """Pull blocks from a pool known only by device pointers (an IPC mapping of a
+    peer process's cache with the destination's layout) into ``dst`` on its device."""
+    _require_cuda(dst_keys, dst_values, src_blocks, dst_blocks)
+    L, dnb, bs, h, d = _cache_geometry(dst_keys)
+    device = dst_keys.device
+    with torch.cuda.device(device):
+        status = lib.nie_copy_blocks(
+            src_keys_ptr,
+            src_values_ptr,
+            src_num_blocks,
+            src_blocks.data_ptr(),
+            dst_keys.data_ptr(),
+            dst_values.data_ptr(),
+            dnb,
+            dst_blocks.data_ptr(),
+            int(num_copy_blocks),
+            int(tail_valid_tokens),
+            dtype_code(dst_keys.dtype),
+            L,
+            bs,
+            h,
+            d,
+            error_flag(device).data_ptr(),
+            _stream(device),
+        )
+    check(status, "nie_copy_blocks")
+    _count()
+
+
+def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """64-byte CUDA IPC handle of the allocation holding ``t`` and ``t``'s offset in it."""
+    _require_cuda(t)
+    handle = (ctypes.c_ubyte * 64)()
+    offset = ctypes.c_uint64()
+    with torch.cuda.device(t.device):
+        check(lib.nie_ipc_export(t.data_ptr(), handle, ctypes.byref(offset)), "nie_ipc_export")
+    return bytes(handle), int(offset.value)
+
+
+def ipc_import(handle: bytes, offset: int, device: torch.device) -> tuple[int, int]:
+    """Map a peer process's allocation on ``device``; returns (pointer, mapping base)."""
+    buf = (ctypes.c_ubyte * 64).from_buffer_copy(handle)
+    ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+    with torch.cuda.device(device):
+        check(lib.nie_ipc_import(buf, offset, ctypes.byref(ptr), ctypes.byref(base)), "nie_ipc_import")
+    return int(ptr.value), int(base.value)
+
+
+def ipc_close(base: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        check(lib.nie_ipc_close(base), "nie_ipc_close")
 
 
 _peer_enabled: set[tuple[int, int]] = set()

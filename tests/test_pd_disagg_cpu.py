@@ -1,0 +1,98 @@
+"""P/D disaggregation protocol across two processes (gloo, CPU, scripted models).
+
+Rank 0 prefills and hands requests off through the TCP store; rank 1 imports (host bookkeeping
+only here), decodes with continuous batching and acknowledges; the prefill
+rank frees each request's blocks on the acknowledgement.  The GPU copy path
+is exercised by tests/test_pd_gpu.py.
+"""
+
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from nano_infer_engine_b200.generation.config import GenerationConfig
+from nano_infer_engine_b200.generation.pd_disagg import (
+    HEADER_WORDS,
+    PairChannel,
+    assign_pairs,
+    run_decode,
+    run_prefill,
+)
+from nano_infer_engine_b200.paged_cache import PagedKVCache
+
+PROMPT_LENS = (5, 17, 1, 33, 8, 40)
+NEW_TOKENS = 4
+
+
+def _prompts():
+    g = torch.Generator().manual_seed(0)
+    return [torch.randint(0, 8, (1, n), generator=g) for n in PROMPT_LENS]
+
+
+def test_router_balances_outstanding_work():
+    work = [100, 10, 10, 10, 90, 5]
+    assert assign_pairs(work, 2) == [[0, 5], [1, 2, 3, 4]]
+    assert assign_pairs(work, 1) == [list(range(6))]
+    assert sorted(sum(assign_pairs(work, 3), [])) == list(range(6))
+
+
+def _worker(rank, port, result_path):
+    from test_scheduler_host import ScriptedModel
+
+    store = dist.TCPStore("127.0.0.1", port, 2, rank == 0, timeout=timedelta(seconds=60))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=2, timeout=timedelta(seconds=60))
+    prompts = _prompts()
+    words = HEADER_WORDS + 16
+    channel = PairChannel(store, rank, 1 - rank, words)
+    schedules = {f"pd-{i}": tuple(range(1, 8)) for i in range(len(prompts))}
+    if rank == 0:
+        cache = PagedKVCache(16, 4, 1, 1, 4, torch.float32, "cpu")  # 16 blocks: forces waiting for ACKs
+        stats = run_prefill(ScriptedModel(schedules), cache, channel, list(enumerate(prompts)), token_budget=40,
+                            idle_sleep=0.001)
+        result = {"requests": stats.requests, "batches": stats.batches, "free": cache.allocator.free_block_count}
+    else:
+        cache = PagedKVCache(64, 4, 1, 1, 4, torch.float32, "cpu")
+
+        def fake_import(c, sid, length, src_blocks):
+            assert len(src_blocks) == -(-length // c.block_size)
+            c.ensure_capacity(sid, length)
+            c.advance(sid, length)
+            return None
+
+        reqs = run_decode(ScriptedModel(schedules), cache, channel, lambda i: prompts[i],
+                          GenerationConfig(max_new_tokens=NEW_TOKENS), 3, fake_import, 8, idle_sleep=0.001)
+        result = {
+            "tokens": {r.sequence_id: r.sequence[0, r.prompt.shape[1]:].tolist() for r in reqs},
+            "status": sorted({r.status.value for r in reqs}),
+            "free": cache.allocator.free_block_count,
+        }
+    torch.save(result, f"{result_path}.{rank}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_prefill_decode_handoff_over_gloo(tmp_path):
+    path = str(tmp_path / "res")
+    mp.start_processes(_worker, args=(_free_port(), path), nprocs=2, start_method="spawn", join=True)
+    pre = torch.load(path + ".0")
+    dec = torch.load(path + ".1")
+    assert pre["requests"] == len(PROMPT_LENS)
+    assert pre["batches"] > 1  # the 40-token budget splits the prompts
+    assert pre["free"] == 16  # every handed-off request was acknowledged and freed
+    assert dec["status"] == ["completed"]
+    assert dec["free"] == 64
+    # first token from the prefill side (its script starts at 1), then the
+    # decode side's script continues from its own start for that sequence
+    assert len(dec["tokens"]) == len(PROMPT_LENS)
+    for toks in dec["tokens"].values():
+        assert len(toks) == NEW_TOKENS and toks[0] == 1
