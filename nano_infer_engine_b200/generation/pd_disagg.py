@@ -25,6 +25,7 @@ injectable so the protocol runs with gloo on CPU in tests.
 
 from __future__ import annotations
 
+import pickle
 import time
 from collections import deque
 from collections.abc import Callable
@@ -134,6 +135,29 @@ def import_pool(exported: dict, cache: PagedKVCache) -> RemotePool:
     return RemotePool(kp, vp, exported["shape"][1], (kb, vb), cache.device)
 
 
+def publish_pool(store, rank: int, cache: PagedKVCache) -> None:
+    """Prefill rank: put its pool's IPC handles in the store for its decode peer."""
+    store.set(f"pd/pool/{rank}", pickle.dumps(export_pool(cache)))
+
+
+def open_peer_pool(store, peer: int, cache: PagedKVCache) -> RemotePool:
+    """Decode rank: map the prefill peer's published pool onto ``cache``'s device."""
+    key = f"pd/pool/{peer}"
+    store.wait([key])
+    return import_pool(pickle.loads(store.get(key)), cache)
+
+
+def close_peer_pool(store, rank: int, remote: RemotePool) -> None:
+    """Decode rank: unmap the peer pool and tell the exporter it may free it."""
+    remote.close()
+    store.set(f"pd/unmapped/{rank}", b"1")
+
+
+def wait_pool_unmapped(store, peer: int) -> None:
+    """Prefill rank: block until the decode peer has unmapped this rank's pool."""
+    store.wait([f"pd/unmapped/{peer}"])
+
+
 def gpu_import(remote: RemotePool):
     """Block import for the decode worker: allocate, pull over NVLink, advance."""
 
@@ -148,7 +172,7 @@ def gpu_import(remote: RemotePool):
                                       cache.values, dst_t, n, length % cache.block_size)
         cache.advance(sequence_id, length)
         event = torch.cuda.Event()
-        event.record()
+        event.record(torch.cuda.current_stream(dev))
         return event
 
     return _import
