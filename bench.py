@@ -16,7 +16,11 @@ prompts U[128, 2048], 256 greedy new tokens each, prefill chunk 128, at most
 * ``cpu_baseline`` - the CPU oracle (restated reference forward) on a bounded
                 sample of the same workload, extrapolated to tokens/s.
 
-N GPUs (torchrun): independent replicas, weak scaling, max-over-ranks time.
+N GPUs (torchrun), N even: N/2 prefill/decode pairs behind the router
+(BASELINE config 5's prompt-length distribution, 16 requests per GPU, closed
+loop, weak scaling, max-over-ranks time); the prefill GPU of a pair hands
+requests off and the decode GPU pulls their KV blocks over NVLink (CUDA IPC).
+Odd N: independent replicas of the 1-GPU run.
 ``--impl reference`` times the reference algorithm on the host cores (the
 oracle port; rank 0 only) for the same metric.
 """
@@ -195,6 +199,177 @@ def time_e2e(model, cache, host_prompts, new_tokens, steps, device):
     stop.record()
     torch.cuda.synchronize()
     return start.elapsed_time(stop) / 1e3, h2d, d2h
+
+
+# ------------------------------------------------------ P/D pairs (N >= 2)
+PD_REQUESTS_PER_GPU = 16
+
+
+def pd_workload(num_requests, seed=SEED):
+    """BASELINE config 5's prompt lengths: log-normal with mean 1024 (sigma 1), capped to [1, 8192]."""
+    g = torch.Generator().manual_seed(seed + 5)
+    lengths = torch.empty(num_requests, dtype=torch.float64).log_normal_(math.log(1024) - 0.5, 1.0, generator=g)
+    lengths = lengths.round().clamp(1, 8192).long().tolist()
+    return [torch.randint(0, 128256, (1, n), generator=g) for n in lengths]
+
+
+class PDRank:
+    """One rank of a prefill/decode pair: even ranks prefill, odd ranks decode.
+
+    The router (``assign_pairs``, least outstanding prompt+output tokens)
+    splits the job's requests over the pairs identically on every rank; the
+    prefill rank's KV pool is mapped into its decode peer with CUDA IPC and
+    blocks are pulled with the block-copy kernel.
+    """
+
+    def __init__(self, dist_ctx, rank, world, device, model, host_prompts, new_tokens):
+        from nano_infer_engine_b200.generation.pd_disagg import (
+            HEADER_WORDS,
+            PairChannel,
+            assign_pairs,
+            gpu_import,
+            open_peer_pool,
+            publish_pool,
+        )
+        from nano_infer_engine_b200.paged_cache import PagedKVCache
+
+        self.device = device
+        self.model = model
+        self.new_tokens = new_tokens
+        self.prefill = rank % 2 == 0
+        self.rank = rank
+        self.peer = rank ^ 1
+        self.store = dist_ctx.distributed_c10d._get_default_store()
+        work = [p.shape[1] + new_tokens for p in host_prompts]
+        self.mine = assign_pairs(work, world // 2)[rank // 2]
+        self.host = {i: host_prompts[i] for i in self.mine}
+        self.resident = {i: p.to(device) for i, p in self.host.items()}
+        longest = max(p.shape[1] for p in host_prompts)
+        self.channel = PairChannel(self.store, rank, self.peer, HEADER_WORDS + -(-longest // 16))
+        blocks = sum(-(-(self.host[i].shape[1] + (0 if self.prefill else new_tokens)) // 16) for i in self.mine)
+        self.cache = PagedKVCache(blocks + 64, 16, 16, 8, 64, torch.bfloat16, device)
+        if self.prefill:
+            publish_pool(self.store, rank, self.cache)
+            self.remote = None
+        else:
+            self.remote = open_peer_pool(self.store, self.peer, self.cache)
+            self.pull = gpu_import(self.remote)
+
+    def step(self, e2e=False):
+        """One closed-loop pass over this pair's requests; returns (h2d bytes, d2h bytes, outputs)."""
+        from nano_infer_engine_b200.generation.config import GenerationConfig
+        from nano_infer_engine_b200.generation.pd_disagg import run_decode, run_prefill
+
+        if e2e:
+            prompts = {i: p.to(self.device, non_blocking=True) for i, p in self.host.items()}
+            h2d = sum(p.numel() * p.element_size() for p in self.host.values())
+        else:
+            prompts, h2d = self.resident, 0
+        if self.prefill:
+            run_prefill(self.model, self.cache, self.channel, [(i, prompts[i]) for i in self.mine],
+                        token_budget=4096, idle_sleep=0.0002)
+            return h2d, 0, None
+        reqs = run_decode(self.model, self.cache, self.channel, prompts.__getitem__,
+                          GenerationConfig(max_new_tokens=self.new_tokens), len(self.mine), self.pull,
+                          self.model.config.vocab_size, idle_sleep=0.0002)
+        if e2e:
+            outs = [r.sequence.to("cpu") for r in reqs]
+            return h2d, sum(o.numel() * o.element_size() for o in outs), outs
+        return h2d, 0, reqs
+
+    def close(self):
+        from nano_infer_engine_b200.generation.pd_disagg import close_peer_pool, wait_pool_unmapped
+
+        if self.remote is not None:
+            close_peer_pool(self.store, self.rank, self.remote)
+        else:
+            wait_pool_unmapped(self.store, self.peer)
+
+
+def time_pd(pd, steps, warmup, dist_ctx, e2e=False):
+    from nano_infer_engine_b200 import ops
+
+    with torch.inference_mode():
+        for _ in range(warmup):
+            pd.step()
+        torch.cuda.synchronize()
+        barrier(dist_ctx)
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches0 = ops.LAUNCHES
+        h2d = d2h = 0
+        start.record()
+        for _ in range(steps):
+            h2d, d2h, _ = pd.step(e2e)
+        stop.record()
+        torch.cuda.synchronize()
+    elapsed = start.elapsed_time(stop) / 1e3
+    totals = torch.tensor([ops.LAUNCHES - launches0, h2d, d2h], dtype=torch.float64, device=pd.device)
+    dist_ctx.all_reduce(totals)
+    return max_over_ranks(dist_ctx, elapsed, pd.device), [int(x) for x in totals.tolist()]
+
+
+def run_pd(args, dist_ctx, rank, local, device, world):
+    """N >= 2 (even): N/2 prefill/decode pairs behind the router, weak scaling
+    (16 requests per GPU), closed loop: one step = every pair generates its batch."""
+    model = build_engine(device)
+    host = [p.pin_memory() for p in pd_workload(PD_REQUESTS_PER_GPU * world)]
+    pd = PDRank(dist_ctx, rank, world, device, model, host, args.new_tokens)
+    with ClockSampler(local) as clocks:
+        elapsed, (launches, _, _) = time_pd(pd, args.steps, args.warmup, dist_ctx)
+    value = len(host) * args.new_tokens * args.steps / elapsed
+    e2e = None
+    if not args.no_e2e:
+        e2e_steps = max(1, args.steps // 2)
+        e2e_s, (_, h2d, d2h) = time_pd(pd, e2e_steps, 0, dist_ctx, e2e=True)
+        e2e = {"value": len(host) * args.new_tokens * e2e_steps / e2e_s, "unit": UNIT,
+               "h2d_bytes_per_step": h2d // e2e_steps, "d2h_bytes_per_step": d2h // e2e_steps}
+    pd.close()
+    del pd
+    torch.cuda.empty_cache()
+    roofline = None
+    if rank == 0 and args.only == "all":
+        dec = decode_config3(device, args.decode_iters, args.decode_batch, args.decode_blocks)
+        peak, peak_kind = measured_peaks()
+        achieved = dec["bytes"] / (dec["ms"] / 1e3) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                    "traffic": ncu_traffic(), "kernel": "decode_tma_kernel + decode_combine_kernel",
+                    "workload": f"config3 decode on rank 0: B=64, sum ctx {dec['sum_ctx']}, "
+                                f"{dec['bytes']} algorithmic bytes/launch",
+                    "ms_per_launch": dec["ms"], "peak_kind": f"{peak_kind} (hbm_gbs burst copy)"}
+    barrier(dist_ctx)
+    if rank == 0:
+        lens = [p.shape[1] for p in host]
+        print(json.dumps({
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed / args.steps * 1e3,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded prompts, random-init weights N(0, 0.02))",
+            "config": {
+                "workload": f"config5 P/D, closed loop: Llama-3.2-1B shape, {PD_REQUESTS_PER_GPU} requests per GPU, "
+                            f"prompts log-normal mean 1024 capped 8192 (sum {sum(lens)}, max {max(lens)}), "
+                            f"{args.new_tokens} greedy new tokens; prefill batches <=4096 tokens; KV blocks pulled "
+                            "over NVLink by the decode GPU",
+                "global_batch": len(host),
+                "parallelism": f"{world // 2} P/D pairs (prefill rank 2k, decode rank 2k+1) behind the router",
+                "l2": "inputs larger than L2 (2.47 GB of weights streamed per decode step)",
+            },
+            "roofline": roofline,
+            "cpu_baseline": None,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }))
+    dist_ctx.barrier()
+    dist_ctx.destroy_process_group()
+    return 0
 
 
 # ------------------------------------------------------ decode roofline
@@ -461,6 +636,9 @@ def main():
     if rank == 0 or dist_ctx is None:
         __graft_entry__.build()
     barrier(dist_ctx)
+    world = dist_ctx.get_world_size() if dist_ctx else 1
+    if world >= 2 and world % 2 == 0 and args.only in ("all", "engine"):
+        return run_pd(args, dist_ctx, rank, local, device, world)
     if args.only == "decode":
         dec = decode_config3(device, args.decode_iters, args.decode_batch, args.decode_blocks)
         peak, _ = measured_peaks()

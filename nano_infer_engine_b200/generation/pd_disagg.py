@@ -272,7 +272,7 @@ def run_decode(
     bs = cache.block_size
     dtype = cache.keys.dtype
     while True:
-        for msg in channel.poll():
+        for msg in () if done else channel.poll():  # nothing follows DONE
             if msg[0] == HANDOFF:
                 index, length, token, nblk = msg[1], msg[2], msg[3], msg[4]
                 sid = f"pd-{index}"
