@@ -84,7 +84,9 @@ class PairChannel:
         self.store.set(self._out + str(self._sent), msg.tobytes())
         self._sent += 1
 
-    def poll(self) -> list[list[int]]:
+    def poll(self, stop_after: int | None = None) -> list[list[int]]:
+        """Every waiting message in order; with ``stop_after``, none past the first
+        message of that type (later ones stay queued, e.g. the next pass's)."""
         out = []
         while True:
             key = self._in + str(self._received)
@@ -93,6 +95,8 @@ class PairChannel:
             out.append(np.frombuffer(self.store.get(key), dtype=np.int64).tolist())
             self.store.delete_key(key)
             self._received += 1
+            if stop_after is not None and out[-1][0] == stop_after:
+                return out
 
     def close(self) -> None:
         """Messages are delivered when ``send`` returns; nothing is left in flight."""
@@ -272,7 +276,7 @@ def run_decode(
     bs = cache.block_size
     dtype = cache.keys.dtype
     while True:
-        for msg in () if done else channel.poll():  # nothing follows DONE
+        for msg in () if done else channel.poll(stop_after=DONE):
             if msg[0] == HANDOFF:
                 index, length, token, nblk = msg[1], msg[2], msg[3], msg[4]
                 sid = f"pd-{index}"

@@ -26,6 +26,7 @@ from nano_infer_engine_b200.paged_cache import PagedKVCache
 
 PROMPT_LENS = (5, 17, 1, 33, 8, 40)
 NEW_TOKENS = 4
+PASSES = 3
 
 
 def _prompts():
@@ -40,6 +41,23 @@ def test_router_balances_outstanding_work():
     assert sorted(sum(assign_pairs(work, 3), [])) == list(range(6))
 
 
+def test_pair_channel_order_and_pass_boundary():
+    store = dist.HashStore()
+    a = PairChannel(store, 0, 1, HEADER_WORDS)
+    b = PairChannel(store, 1, 0, HEADER_WORDS)
+    assert b.poll() == []
+    for msg in ([1, 7], [3, 1], [1, 8]):
+        a.send(msg)
+    pad = [0] * (HEADER_WORDS - 2)
+    assert b.poll(stop_after=3) == [[1, 7, *pad], [3, 1, *pad]]  # the next pass's record stays queued
+    assert b.poll() == [[1, 8, *pad]]
+    assert b.poll() == []
+    b.send([2, 5])
+    assert a.poll() == [[2, 5, *pad]]
+    with pytest.raises(ValueError, match="fixed size"):
+        a.send([0] * (HEADER_WORDS + 1))
+
+
 def _worker(rank, port, result_path):
     from test_scheduler_host import ScriptedModel
 
@@ -51,8 +69,9 @@ def _worker(rank, port, result_path):
     schedules = {f"pd-{i}": tuple(range(1, 8)) for i in range(len(prompts))}
     if rank == 0:
         cache = PagedKVCache(16, 4, 1, 1, 4, torch.float32, "cpu")  # 16 blocks: forces waiting for ACKs
-        stats = run_prefill(ScriptedModel(schedules), cache, channel, list(enumerate(prompts)), token_budget=40,
-                            idle_sleep=0.001)
+        for _ in range(PASSES):  # passes reuse the channel, the caches and the sequence ids
+            stats = run_prefill(ScriptedModel(schedules), cache, channel, list(enumerate(prompts)), token_budget=40,
+                                idle_sleep=0.001)
         result = {"requests": stats.requests, "batches": stats.batches, "free": cache.allocator.free_block_count}
     else:
         cache = PagedKVCache(64, 4, 1, 1, 4, torch.float32, "cpu")
@@ -63,8 +82,9 @@ def _worker(rank, port, result_path):
             c.advance(sid, length)
             return None
 
-        reqs = run_decode(ScriptedModel(schedules), cache, channel, lambda i: prompts[i],
-                          GenerationConfig(max_new_tokens=NEW_TOKENS), 3, fake_import, 8, idle_sleep=0.001)
+        for _ in range(PASSES):
+            reqs = run_decode(ScriptedModel(schedules), cache, channel, lambda i: prompts[i],
+                              GenerationConfig(max_new_tokens=NEW_TOKENS), 3, fake_import, 8, idle_sleep=0.001)
         result = {
             "tokens": {r.sequence_id: r.sequence[0, r.prompt.shape[1]:].tolist() for r in reqs},
             "status": sorted({r.status.value for r in reqs}),

@@ -6,7 +6,8 @@
   process maps the prefill pool with CUDA IPC and pulls each request's blocks
   with the same kernel.  The KV bytes on both sides must be identical and
   the greedy tokens must equal a single-GPU run of the same model (fp32, so
-  that batching differences cannot flip a token).
+  that batching differences cannot flip a token).  Two passes over the same
+  requests reuse the channel, both pools and the sequence ids.
 
 Both tests skip on a box with fewer than two GPUs.
 """
@@ -23,6 +24,7 @@ pytestmark = pytest.mark.gpu
 
 PROMPT_LENS = (5, 40, 77, 16, 130, 300, 1, 64)
 NEW_TOKENS = 12
+PASSES = 2
 
 
 def _need_two_gpus():
@@ -115,8 +117,9 @@ def _pair_worker(rank, port, out):
 
         cache.release = release_and_record
         with torch.inference_mode():
-            stats = run_prefill(model, cache, channel, list(enumerate(prompts)), token_budget=256,
-                                idle_sleep=0.0005)
+            for _ in range(PASSES):  # passes reuse the channel, both pools and the sequence ids
+                stats = run_prefill(model, cache, channel, list(enumerate(prompts)), token_budget=256,
+                                    idle_sleep=0.0005)
         ops.check_device_errors(dev)
         wait_pool_unmapped(store, 1)
         result = {"kv": saved, "batches": stats.batches, "free": cache.allocator.free_block_count}
@@ -132,8 +135,10 @@ def _pair_worker(rank, port, out):
             return event
 
         with torch.inference_mode():
-            reqs = run_decode(model, cache, channel, lambda i: prompts[i], GenerationConfig(max_new_tokens=NEW_TOKENS),
-                              4, pull_and_record, cfg.vocab_size, idle_sleep=0.0005)
+            for _ in range(PASSES):
+                reqs = run_decode(model, cache, channel, lambda i: prompts[i],
+                                  GenerationConfig(max_new_tokens=NEW_TOKENS), 4, pull_and_record, cfg.vocab_size,
+                                  idle_sleep=0.0005)
         ops.check_device_errors(dev)
         close_peer_pool(store, 1, remote)
         result = {
