@@ -59,9 +59,12 @@ def parse_args():
     p.add_argument("--decode-iters", type=int, default=20)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--only", choices=("all", "engine", "decode", "mixed"), default="all",
+    p.add_argument("--only", choices=("all", "engine", "decode", "mixed", "pd-open"), default="all",
                    help="engine: headline run only; decode: config-3 decode micro-bench only; "
-                        "mixed: config-4 mixed step only (profiling)")
+                        "mixed: config-4 mixed step only (profiling); pd-open: config 5 open loop "
+                        "(Poisson arrivals, TTFT/TPOT, transfer GB/s; even N >= 2)")
+    p.add_argument("--pd-requests", type=int, default=512)
+    p.add_argument("--pd-rate", type=float, default=20.0)
     p.add_argument("--decode-batch", type=int, default=64)
     p.add_argument("--decode-blocks", type=int, default=131072)
     return p.parse_args()
@@ -253,25 +256,31 @@ class PDRank:
             self.remote = None
         else:
             self.remote = open_peer_pool(self.store, self.peer, self.cache)
-            self.pull = gpu_import(self.remote)
+            self.transfers = []
+            self.pull = gpu_import(self.remote, self.transfers)
 
-    def step(self, e2e=False):
-        """One closed-loop pass over this pair's requests; returns (h2d bytes, d2h bytes, outputs)."""
+    def step(self, e2e=False, indices=None, arrival=None, clock=time.perf_counter, record=None):
+        """One pass over this pair's requests (``indices``: a subset, in order);
+        returns (h2d bytes, d2h bytes, outputs).  ``arrival`` maps request index
+        to seconds after the pass starts (open loop); ``record`` collects
+        first-token times (prefill rank) or (hand-off, completion) times (decode rank)."""
         from nano_infer_engine_b200.generation.config import GenerationConfig
         from nano_infer_engine_b200.generation.pd_disagg import run_decode, run_prefill
 
+        mine = self.mine if indices is None else indices
         if e2e:
-            prompts = {i: p.to(self.device, non_blocking=True) for i, p in self.host.items()}
-            h2d = sum(p.numel() * p.element_size() for p in self.host.values())
+            prompts = {i: self.host[i].to(self.device, non_blocking=True) for i in mine}
+            h2d = sum(self.host[i].numel() * self.host[i].element_size() for i in mine)
         else:
             prompts, h2d = self.resident, 0
         if self.prefill:
-            run_prefill(self.model, self.cache, self.channel, [(i, prompts[i]) for i in self.mine],
-                        token_budget=4096, idle_sleep=0.0002)
+            run_prefill(self.model, self.cache, self.channel, [(i, prompts[i]) for i in mine],
+                        token_budget=4096, idle_sleep=0.0002, clock=clock,
+                        arrival=None if arrival is None else [arrival[i] for i in mine], first_token_at=record)
             return h2d, 0, None
         reqs = run_decode(self.model, self.cache, self.channel, prompts.__getitem__,
-                          GenerationConfig(max_new_tokens=self.new_tokens), len(self.mine), self.pull,
-                          self.model.config.vocab_size, idle_sleep=0.0002)
+                          GenerationConfig(max_new_tokens=self.new_tokens), len(mine), self.pull,
+                          self.model.config.vocab_size, idle_sleep=0.0002, clock=clock, timings=record)
         if e2e:
             outs = [r.sequence.to("cpu") for r in reqs]
             return h2d, sum(o.numel() * o.element_size() for o in outs), outs
@@ -365,6 +374,83 @@ def run_pd(args, dist_ctx, rank, local, device, world):
             "cpu_baseline": None,
             "e2e": e2e,
             "gpu_launches": launches,
+            "clocks": clocks.summary(),
+        }))
+    dist_ctx.barrier()
+    dist_ctx.destroy_process_group()
+    return 0
+
+
+def pd_open_workload(num_requests, rate, seed=SEED):
+    """Config 5: log-normal prompts and Poisson arrivals (seeded exponential gaps)."""
+    prompts = pd_workload(num_requests, seed)
+    g = torch.Generator().manual_seed(seed + 9)
+    gaps = torch.empty(num_requests, dtype=torch.float64).exponential_(rate, generator=g)
+    return prompts, gaps.cumsum(0).tolist()
+
+
+def _pct(values, q):
+    values = sorted(values)
+    return values[min(len(values) - 1, int(q * len(values)))] if values else None
+
+
+def run_pd_open(args, dist_ctx, rank, local, device, world):
+    """Config 5 open loop on N/2 pairs: output tok/s (arrival-capped), TTFT, TPOT, transfer GB/s."""
+    model = build_engine(device)
+    host, arrival = pd_open_workload(args.pd_requests, args.pd_rate)
+    host = [p.pin_memory() for p in host]
+    pd = PDRank(dist_ctx, rank, world, device, model, host, args.new_tokens)
+    with torch.inference_mode():
+        pd.step(indices=pd.mine[:16])  # warm-up: graphs, workspaces, allocator
+        if not pd.prefill:
+            pd.transfers.clear()
+        torch.cuda.synchronize()
+        barrier(dist_ctx)
+        t0 = time.monotonic()
+        record = {}
+        with ClockSampler(local) as clocks:
+            pd.step(arrival=arrival, clock=lambda: time.monotonic() - t0, record=record)
+        torch.cuda.synchronize()
+        elapsed = time.monotonic() - t0
+    elapsed = max_over_ranks(dist_ctx, elapsed, device)
+    # gather per-request timings and transfer records on rank 0 through the store
+    store = dist_ctx.distributed_c10d._get_default_store()
+    if pd.prefill:
+        mine = {i: record[i] - arrival[i] for i in pd.mine}
+    else:
+        moved = [(b, s.elapsed_time(e) / 1e3) for b, s, e in pd.transfers]
+        tpot = {i: (t1 - t0_) / max(1, args.new_tokens - 1) for i, (t0_, t1) in record.items()}
+        mine = {"tpot": tpot, "transfers": moved}
+    store.set(f"pdopen/{rank}", json.dumps(mine))
+    pd.close()
+    barrier(dist_ctx)
+    if rank == 0:
+        ttft, tpot, moved = [], [], []
+        for r in range(world):
+            data = json.loads(store.get(f"pdopen/{r}"))
+            if r % 2 == 0:
+                ttft.extend(data.values())
+            else:
+                tpot.extend(data["tpot"].values())
+                moved.extend(data["transfers"])
+        per = [b / t / 1e9 for b, t in moved if t > 0]
+        print(json.dumps({
+            "mode": "pd-open (config 5)",
+            "n_gpus": world,
+            "pairs": world // 2,
+            "requests": args.pd_requests,
+            "rate_req_s": args.pd_rate,
+            "new_tokens": args.new_tokens,
+            "output_tok_s": args.pd_requests * args.new_tokens / elapsed,
+            "arrival_cap_tok_s": args.pd_rate * args.new_tokens,
+            "duration_s": elapsed,
+            "ttft_ms": {"p50": 1e3 * _pct(ttft, 0.5), "p90": 1e3 * _pct(ttft, 0.9), "p99": 1e3 * _pct(ttft, 0.99)},
+            "tpot_ms": {"p50": 1e3 * _pct(tpot, 0.5), "p90": 1e3 * _pct(tpot, 0.9), "p99": 1e3 * _pct(tpot, 0.99)},
+            "transfer": {"count": len(moved), "bytes_total": sum(b for b, _ in moved),
+                         "gbs_median": _pct(per, 0.5), "gbs_aggregate": sum(b for b, _ in moved) /
+                         max(1e-12, sum(t for _, t in moved)) / 1e9,
+                         "note": "bytes of the copied blocks (K+V, all layers) / copy-kernel event time on the "
+                                 "decode GPU; reads cross NVLink from the prefill GPU's pool"},
             "clocks": clocks.summary(),
         }))
     dist_ctx.barrier()
@@ -637,6 +723,10 @@ def main():
         __graft_entry__.build()
     barrier(dist_ctx)
     world = dist_ctx.get_world_size() if dist_ctx else 1
+    if world >= 2 and world % 2 == 0 and args.only == "pd-open":
+        return run_pd_open(args, dist_ctx, rank, local, device, world)
+    if args.only == "pd-open":
+        raise SystemExit("--only pd-open needs an even number of GPUs >= 2 under torchrun")
     if world >= 2 and world % 2 == 0 and args.only in ("all", "engine"):
         return run_pd(args, dist_ctx, rank, local, device, world)
     if args.only == "decode":

@@ -162,21 +162,32 @@ def wait_pool_unmapped(store, peer: int) -> None:
     store.wait([f"pd/unmapped/{peer}"])
 
 
-def gpu_import(remote: RemotePool):
-    """Block import for the decode worker: allocate, pull over NVLink, advance."""
+def gpu_import(remote: RemotePool, transfer_log: list | None = None):
+    """Block import for the decode worker: allocate, pull over NVLink, advance.
+
+    With ``transfer_log``, each pull appends ``(bytes moved, start event, end
+    event)`` (timing events on the decode stream around the copy kernel).
+    """
 
     def _import(cache: PagedKVCache, sequence_id: str, length: int, src_blocks: list[int]):
         n = -(-length // cache.block_size)
         cache.ensure_capacity(sequence_id, length)
         dst = cache.get_block_table(sequence_id)[:n]
         dev = cache.device
+        stream = torch.cuda.current_stream(dev)
         src_t = torch.tensor(src_blocks[:n], dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
         dst_t = torch.tensor(dst, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        if transfer_log is not None:
+            begin = torch.cuda.Event(enable_timing=True)
+            begin.record(stream)
         ops.copy_blocks_from_pointers(remote.keys_ptr, remote.values_ptr, remote.num_blocks, src_t, cache.keys,
                                       cache.values, dst_t, n, length % cache.block_size)
         cache.advance(sequence_id, length)
-        event = torch.cuda.Event()
-        event.record(torch.cuda.current_stream(dev))
+        event = torch.cuda.Event(enable_timing=transfer_log is not None)
+        event.record(stream)
+        if transfer_log is not None:
+            moved = 2 * n * cache.num_layers * cache.block_size * cache.kv_head_num * cache.head_dim
+            transfer_log.append((moved * cache.keys.element_size(), begin, event))
         return event
 
     return _import
@@ -199,13 +210,16 @@ def run_prefill(
     arrival: list[float] | None = None,
     clock: Callable[[], float] = time.perf_counter,
     idle_sleep: float = 0.0,
+    first_token_at: dict[int, float] | None = None,
 ) -> PrefillStats:
     """Prefill ``(index, prompt[1, n])`` requests in order and hand them to the decode peer.
 
     Batches are formed from arrived requests up to ``token_budget`` prompt
     tokens and the free blocks of ``cache``; a request's blocks are held
     until the decode peer acknowledges its copy.  ``arrival`` (seconds from
-    the start, same order as ``requests``) gates admission for open-loop runs.
+    the start, same order as ``requests``) gates admission for open-loop runs;
+    ``first_token_at`` receives, per request index, the ``clock()`` time at
+    which its first token was known.
     """
     stats = PrefillStats()
     pending = deque(range(len(requests)))
@@ -242,6 +256,10 @@ def run_prefill(
         with torch.inference_mode():
             logits = paged_prefill_chunks(model, chunks, cache, ids)
             first = logits.argmax(dim=-1).tolist()  # also waits for the KV writes
+        if first_token_at is not None:
+            now = clock()
+            for k in batch:
+                first_token_at[requests[k][0]] = now
         for k, sid, tok in zip(batch, ids, first):
             index, prompt = requests[k]
             table = cache.get_block_table(sid)
@@ -266,12 +284,19 @@ def run_decode(
     vocab_size: int,
     *,
     idle_sleep: float = 0.0,
+    clock: Callable[[], float] = time.perf_counter,
+    timings: dict[int, tuple[float, float]] | None = None,
 ) -> list[PagedRequest]:
-    """Receive hand-offs, import their KV, and decode them with continuous batching."""
+    """Receive hand-offs, import their KV, and decode them with continuous batching.
+
+    ``timings`` receives, per request index, the ``clock()`` times at which
+    its hand-off arrived and at which it completed.
+    """
     sched = ContinuousBatchingScheduler(model, config, cache, max_batch_size)
     ready: deque[tuple[PagedRequest, torch.Tensor]] = deque()
     copies: deque[tuple[object, int]] = deque()
     requests: list[PagedRequest] = []
+    received: dict[str, tuple[int, float]] = {}
     done = False
     bs = cache.block_size
     dtype = cache.keys.dtype
@@ -280,6 +305,8 @@ def run_decode(
             if msg[0] == HANDOFF:
                 index, length, token, nblk = msg[1], msg[2], msg[3], msg[4]
                 sid = f"pd-{index}"
+                if timings is not None:
+                    received[sid] = (index, clock())
                 event = import_fn(cache, sid, length, msg[HEADER_WORDS : HEADER_WORDS + nblk])
                 prompt = prompt_of(index)
                 required = (length + config.max_new_tokens - 1 + bs - 1) // bs
@@ -301,7 +328,12 @@ def run_decode(
             sched.add_prefilled_request(request, logits)
             requests.append(request)
         if sched.has_work:
-            sched.step()
+            out = sched.step()
+            if timings is not None and out.terminal_requests:
+                now = clock()
+                for r in out.terminal_requests:
+                    index, t0 = received[r.sequence_id]
+                    timings[index] = (t0, now)
         elif done and not ready and not copies:
             break
         elif idle_sleep:

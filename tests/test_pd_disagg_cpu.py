@@ -70,9 +70,11 @@ def _worker(rank, port, result_path):
     if rank == 0:
         cache = PagedKVCache(16, 4, 1, 1, 4, torch.float32, "cpu")  # 16 blocks: forces waiting for ACKs
         for _ in range(PASSES):  # passes reuse the channel, the caches and the sequence ids
+            first = {}
             stats = run_prefill(ScriptedModel(schedules), cache, channel, list(enumerate(prompts)), token_budget=40,
-                                idle_sleep=0.001)
-        result = {"requests": stats.requests, "batches": stats.batches, "free": cache.allocator.free_block_count}
+                                idle_sleep=0.001, first_token_at=first)
+        result = {"requests": stats.requests, "batches": stats.batches, "free": cache.allocator.free_block_count,
+                  "first": sorted(first)}
     else:
         cache = PagedKVCache(64, 4, 1, 1, 4, torch.float32, "cpu")
 
@@ -83,12 +85,15 @@ def _worker(rank, port, result_path):
             return None
 
         for _ in range(PASSES):
+            timings = {}
             reqs = run_decode(ScriptedModel(schedules), cache, channel, lambda i: prompts[i],
-                              GenerationConfig(max_new_tokens=NEW_TOKENS), 3, fake_import, 8, idle_sleep=0.001)
+                              GenerationConfig(max_new_tokens=NEW_TOKENS), 3, fake_import, 8, idle_sleep=0.001,
+                              timings=timings)
         result = {
             "tokens": {r.sequence_id: r.sequence[0, r.prompt.shape[1]:].tolist() for r in reqs},
             "status": sorted({r.status.value for r in reqs}),
             "free": cache.allocator.free_block_count,
+            "timings": timings,
         }
     torch.save(result, f"{result_path}.{rank}")
     dist.barrier()
@@ -111,6 +116,9 @@ def test_prefill_decode_handoff_over_gloo(tmp_path):
     assert pre["free"] == 16  # every handed-off request was acknowledged and freed
     assert dec["status"] == ["completed"]
     assert dec["free"] == 64
+    assert pre["first"] == list(range(len(PROMPT_LENS)))
+    assert sorted(dec["timings"]) == list(range(len(PROMPT_LENS)))
+    assert all(t1 >= t0 for t0, t1 in dec["timings"].values())
     # first token from the prefill side (its script starts at 1), then the
     # decode side's script continues from its own start for that sequence
     assert len(dec["tokens"]) == len(PROMPT_LENS)
