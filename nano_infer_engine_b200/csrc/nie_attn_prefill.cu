@@ -284,7 +284,10 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       const bool masked = key0 + kPfBN - 1 > diag_from;
       // v holds the rounded scores in the "raw" domain (before * scale*log2e,
       // a positive factor, so the max can be taken before scaling)
-      float mx_raw = -INFINITY;
+      // eight independent max chains (a single chain is 32 dependent ops)
+      float mxa[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mxa[i] = -INFINITY;
       if (a.scale_pow2) {
         // bf16(bf16(acc) * 2^k) == bf16(acc) * 2^k: one rounding
 #pragma unroll
@@ -297,7 +300,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           }
           v[e] = __float_as_uint(x0);
           v[e + 1] = __float_as_uint(x1);
-          mx_raw = fmaxf(mx_raw, fmaxf(x0, x1));
+          mxa[(e >> 1) & 7] = fmaxf(mxa[(e >> 1) & 7], fmaxf(x0, x1));
         }
       } else {
 #pragma unroll
@@ -315,17 +318,12 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           }
           v[e] = __float_as_uint(x0);
           v[e + 1] = __float_as_uint(x1);
-          mx_raw = fmaxf(mx_raw, fmaxf(x0, x1));
+          mxa[(e >> 1) & 7] = fmaxf(mxa[(e >> 1) & 7], fmaxf(x0, x1));
         }
       }
+      const float mx_raw = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                                 fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
       const float mx = mx_raw * a.scale_log2e;
-      // O of the previous tile must be complete before it is rescaled (and
-      // every phase of o_done is consumed in order)
-      if (j >= 1 && !pf_wait(b, &b->o_done, (uint32_t)(j - 1) & 1u, a.err)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
       const bool raise = mx > m_ref + kRescaleLog2;
       if (__any_sync(0xffffffffu, raise)) {
         const float alpha = raise ? fast_exp2(m_ref - mx) : 1.f;
@@ -334,6 +332,15 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           m_ref = mx;
         }
         if (j >= 1) {
+          // O must hold P_{j-1} V_{j-1} before it is rescaled.  S_j was issued
+          // after P_{j-2} V_{j-2} and its commit covers every earlier MMA, so
+          // o_done has completed j-1 or j phases here: the parity wait for
+          // phase j-1 is unambiguous although earlier phases were not waited on.
+          if (!pf_wait(b, &b->o_done, (uint32_t)(j - 1) & 1u, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           uint32_t o[32];
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
@@ -345,7 +352,9 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           }
         }
       }
-      float rs0 = 0.f, rs1 = 0.f;
+      float rsa[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rsa[i] = 0.f;
       uint32_t pk[32];
       // a row whose keys in this chunk are all masked keeps m_ref = -inf: its
       // p must come out 0, not exp2(-inf + inf)
@@ -354,18 +363,19 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       for (int e = 0; e < 32; ++e) {
         const float p0 = fast_exp2(fmaf(__uint_as_float(v[2 * e]), sl2e, neg_m));
         const float p1 = fast_exp2(fmaf(__uint_as_float(v[2 * e + 1]), sl2e, neg_m));
-        rs0 += p0;
-        rs1 += p1;
+        rsa[e & 7] += p0 + p1;
         pk[e] = pack_bf16x2(p0, p1);
       }
-      const float rs = rs0 + rs1;
+      const float rs = ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3])) + ((rsa[4] + rsa[5]) + (rsa[6] + rsa[7]));
       tmem_st32(s_addr, pk);
       tmem_wait_st();
       l += rs;
       tc_fence_before();
       mbar_arrive(&b->p_full[sb]);
     }
-    if (ok && n_kt > 0) ok = pf_wait(b, &b->o_done, (uint32_t)(n_kt - 1) & 1u, a.err);
+    // every MMA of the CTA has completed once `done` fires (its single phase is
+    // unambiguous; o_done may be any number of phases behind the last tile)
+    if (ok && n_kt > 0) ok = pf_wait(b, &b->done, 0u, a.err);
     if (ok) {
       tc_fence_after();
       tmem_ld32(tbase + lane_off + kOCol, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
