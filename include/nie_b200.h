@@ -45,6 +45,7 @@ extern "C" {
 #define NIE_DEV_ERR_SLOT_RANGE 2  /* slot outside [0, num_blocks*block_size) */
 #define NIE_DEV_ERR_TIMEOUT 4     /* a bounded wait on an mbarrier ran out */
 #define NIE_DEV_ERR_CAPACITY 8    /* position beyond the block table row */
+#define NIE_DEV_ERR_INDEX_RANGE 16 /* token id outside [0, vocab) */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int nie_version(void);
@@ -302,6 +303,32 @@ int nie_rope_write_kv(const void* q, int64_t q_stride, const void* k,
 int nie_silu_mul(const void* gate, int64_t gate_stride, const void* up,
                  int64_t up_stride, void* out, int64_t rows, int32_t cols,
                  int32_t dtype, void* stream);
+
+/*
+ * nie_embed_rows: out[t] = table[ids[t]] for t < num_tokens, a bit-exact
+ * copy of rows of the [vocab, hidden] embedding table (the nn.Embedding
+ * lookup of models/llama.py:269 and :381).  ids are int64 (device); an id
+ * outside [0, vocab) gives a zero row and NIE_DEV_ERR_INDEX_RANGE.  Rows
+ * must be a multiple of 16 bytes; table and out 16-byte aligned.
+ */
+int nie_embed_rows(const int64_t* ids, int64_t num_tokens, const void* table,
+                   int64_t vocab, int32_t hidden, int32_t dtype, void* out,
+                   int32_t* err_flag, void* stream);
+
+/*
+ * nie_argmax_rows: out[r] = torch.argmax(logits[r]) for r < rows <= 4096:
+ * the first index of the row maximum, NaN ranking above every number (the
+ * greedy sampling of generation/scheduler.py:400 and :505).
+ * Rows of `cols` elements at `row_stride`.  The workspace
+ * (nie_argmax_workspace_size bytes, 256-byte aligned, fixed layout) must be
+ * zero before its first use; the kernel leaves its counters at zero.  Calls
+ * sharing a workspace must not overlap on the GPU.
+ */
+size_t nie_argmax_workspace_size(void);
+
+int nie_argmax_rows(const void* logits, int64_t rows, int64_t cols,
+                    int64_t row_stride, int32_t dtype, int64_t* out,
+                    void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -25,6 +25,7 @@ NIE_DEV_ERR_BLOCK_RANGE = 1
 NIE_DEV_ERR_SLOT_RANGE = 2
 NIE_DEV_ERR_TIMEOUT = 4
 NIE_DEV_ERR_CAPACITY = 8
+NIE_DEV_ERR_INDEX_RANGE = 16
 
 # name -> (restype, argtypes); mirrors include/nie_b200.h one to one.
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
@@ -81,6 +82,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         + [c_int32, c_void_p, c_void_p, c_void_p],
     ),
     "nie_silu_mul": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
+    "nie_embed_rows": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
+    "nie_argmax_workspace_size": (c_size_t, []),
+    "nie_argmax_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
     "nie_varlen_workspace_size": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "nie_varlen_attention": (
         c_int,

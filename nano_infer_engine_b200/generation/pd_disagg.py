@@ -255,7 +255,8 @@ def run_prefill(
         chunks = tuple(requests[k][1] for k in batch)
         with torch.inference_mode():
             logits = paged_prefill_chunks(model, chunks, cache, ids)
-            first = logits.argmax(dim=-1).tolist()  # also waits for the KV writes
+            picked = ops.argmax_rows(logits) if logits.is_cuda else logits.argmax(dim=-1)
+            first = picked.tolist()  # also waits for the KV writes
         if first_token_at is not None:
             now = clock()
             for k in batch:

@@ -21,6 +21,7 @@ from collections import deque
 
 import torch
 
+from .. import ops
 from ..paged_cache import PagedKVCache
 from .config import GenerationConfig
 from .events import SchedulerStepOutput, TokenEvent
@@ -297,7 +298,11 @@ class ContinuousBatchingScheduler:
         if not rows:
             empty = torch.empty((0, 1), dtype=torch.long, device=self.paged_cache.keys.device)
             return empty, []
-        next_tokens = torch.stack(rows).argmax(dim=-1, keepdim=True)
+        stacked = torch.stack(rows)
+        if stacked.is_cuda and stacked.ndim == 2 and len(rows) <= ops.ARGMAX_MAX_ROWS:
+            next_tokens = ops.argmax_rows(stacked).unsqueeze(-1)  # one launch, torch.argmax's answer
+        else:
+            next_tokens = stacked.argmax(dim=-1, keepdim=True)
         return next_tokens, next_tokens.squeeze(-1).tolist()
 
     def _retire(

@@ -232,7 +232,8 @@ class Llama3_2(nn.Module):
         add+norm, gate/up GEMMs, SiLU*up, down GEMM.
         """
         self._ensure_fused()
-        x = self.embed(input_ids)
+        table = self.embed.weight
+        x = ops.embed_rows(input_ids, table) if ops.embed_eligible(table) else self.embed(input_ids)
         positions = meta.positions if rope_positions is None else rope_positions
         sin, cos = self.rope.sin_cos(positions, x.dtype)
         first = self.decoders[0].pre_norm

@@ -16,6 +16,7 @@ import torch
 from ._native import (
     NIE_DEV_ERR_BLOCK_RANGE,
     NIE_DEV_ERR_CAPACITY,
+    NIE_DEV_ERR_INDEX_RANGE,
     NIE_DEV_ERR_SLOT_RANGE,
     NIE_DEV_ERR_TIMEOUT,
     NIE_DTYPE_BF16,
@@ -85,6 +86,7 @@ _ERR_NAMES = {
     NIE_DEV_ERR_SLOT_RANGE: "slot outside the cache",
     NIE_DEV_ERR_TIMEOUT: "bounded mbarrier wait timed out",
     NIE_DEV_ERR_CAPACITY: "token position exceeds the block table",
+    NIE_DEV_ERR_INDEX_RANGE: "token id outside the vocabulary",
 }
 
 
@@ -687,5 +689,72 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
         _stream(gate.device),
     )
     check(status, "nie_silu_mul")
+    _count()
+    return out
+
+
+# ----------------------------------------------------- embedding / sampling
+def embed_rows(ids: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+    """``table[ids]`` for int64 token ids ``[T]`` (the nn.Embedding lookup), bit-exact."""
+    _require_cuda(ids, table)
+    if ids.dtype != torch.int64 or ids.ndim != 1:
+        raise ValueError("ids must be a 1-D int64 tensor")
+    if table.ndim != 2 or not table.is_contiguous():
+        raise ValueError("table must be a contiguous [vocab, hidden] tensor")
+    ids = ids.contiguous()
+    out = torch.empty((ids.shape[0], table.shape[1]), dtype=table.dtype, device=table.device)
+    status = lib.nie_embed_rows(
+        ids.data_ptr(),
+        ids.shape[0],
+        table.data_ptr(),
+        table.shape[0],
+        table.shape[1],
+        dtype_code(table.dtype),
+        out.data_ptr(),
+        error_flag(table.device).data_ptr(),
+        _stream(table.device),
+    )
+    check(status, "nie_embed_rows")
+    _count()
+    return out
+
+
+def embed_eligible(table: torch.Tensor) -> bool:
+    return table.is_cuda and table.dtype in _DTYPES and table.is_contiguous() and (
+        table.shape[1] * table.element_size()) % 16 == 0 and table.data_ptr() % 16 == 0
+
+
+_argmax_ws: dict[int, torch.Tensor] = {}
+ARGMAX_MAX_ROWS = 4096
+
+
+def argmax_rows(logits: torch.Tensor) -> torch.Tensor:
+    """``logits.argmax(dim=-1)`` for ``[R, V]`` rows (R <= 4096): first index of the
+    maximum, NaN ranking highest, as torch.argmax.  One launch; int64 ``[R]``."""
+    _require_cuda(logits)
+    if logits.ndim != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be [rows, cols] with unit inner stride")
+    rows, cols = logits.shape
+    if rows > ARGMAX_MAX_ROWS:
+        raise ValueError(f"at most {ARGMAX_MAX_ROWS} rows")
+    index = logits.device.index if logits.device.index is not None else torch.cuda.current_device()
+    ws = _argmax_ws.get(index)
+    if ws is None:
+        # fixed layout, zeroed once; CUDA graphs may capture its address
+        ws = torch.zeros(int(lib.nie_argmax_workspace_size()), dtype=torch.uint8, device=logits.device)
+        _argmax_ws[index] = ws
+    out = torch.empty(rows, dtype=torch.int64, device=logits.device)
+    status = lib.nie_argmax_rows(
+        logits.data_ptr(),
+        rows,
+        cols,
+        logits.stride(0),
+        dtype_code(logits.dtype),
+        out.data_ptr(),
+        ws.data_ptr(),
+        ws.numel(),
+        _stream(logits.device),
+    )
+    check(status, "nie_argmax_rows")
     _count()
     return out

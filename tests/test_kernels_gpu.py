@@ -381,3 +381,65 @@ def test_fused_silu_mul_and_add_rmsnorm_match_torch_ops(cuda, dtype):
     torch.testing.assert_close(out.float(), norm(x + r).float(), atol=tol, rtol=tol)
     _, plain = ops().add_rmsnorm(x, None, norm.weight, 1e-5)
     torch.testing.assert_close(plain.float(), norm(x).float(), atol=tol, rtol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_kernels_unaligned_fallbacks_match_torch(cuda, dtype):
+    """Shapes and views that are not 16-byte aligned take the scalar kernels: same results."""
+    from nano_infer_engine_b200.layers.rms_norm import RmsNorm
+    from nano_infer_engine_b200.layers.rope import RopeScale, apply_rotary
+
+    g = torch.Generator().manual_seed(52)
+    gate = torch.randn(5, 8190, generator=g).to(dtype).to(cuda)
+    up = torch.randn(5, 8190, generator=g).to(dtype).to(cuda)
+    assert torch.equal(ops().silu_mul(gate, up), torch.nn.functional.silu(gate) * up)
+    x = torch.randn(5, 2046, generator=g).to(dtype).to(cuda)
+    norm = RmsNorm(2046, 1e-5).to(cuda).to(dtype)
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    _, out = ops().add_rmsnorm(x, None, norm.weight, 1e-5)
+    torch.testing.assert_close(out.float(), norm(x).float(), atol=tol, rtol=tol)
+    T, hq, hkv, d = 9, 4, 2, 64
+    base = torch.randn(T, hq * d + 1, generator=g).to(dtype).to(cuda)
+    q = base[:, 1:]  # 2- or 4-byte offset: scalar path
+    k = torch.randn(T, hkv * d, generator=g).to(dtype).to(cuda)
+    v = torch.randn(T, hkv * d, generator=g).to(dtype).to(cuda)
+    sin, cos = RopeScale(d).sin_cos(torch.arange(T, device=cuda) * 7, dtype)
+    kc = torch.zeros(1, 4, 16, hkv, d, dtype=dtype, device=cuda)
+    vc = torch.zeros_like(kc)
+    slots = torch.arange(T, device=cuda) * 3
+    qr = ops().rope_write_kv(q, k, v, sin, cos, kc, vc, 0, slots, hq)
+    assert torch.equal(qr, apply_rotary(q.reshape(T, hq, d), sin, cos))
+    assert torch.equal(kc[0].view(-1, hkv, d)[slots], apply_rotary(k.view(T, hkv, d), sin, cos))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_embed_rows_bit_exact_and_bad_id_flag(cuda, dtype):
+    g = torch.Generator().manual_seed(53)
+    table = torch.randn(1000, 256, generator=g).to(dtype).to(cuda)
+    ids = torch.randint(0, 1000, (37,), generator=g).to(cuda)
+    assert torch.equal(ops().embed_rows(ids, table), torch.nn.functional.embedding(ids, table))
+    bad = torch.tensor([3, 1000, -1, 7], device=cuda)
+    out = ops().embed_rows(bad, table)
+    assert torch.equal(out[0], table[3]) and torch.equal(out[3], table[7])
+    assert not out[1].any() and not out[2].any()
+    with pytest.raises(RuntimeError, match="token id outside the vocabulary"):
+        ops().check_device_errors(cuda)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rows,cols", [(1, 7), (16, 128256), (64, 1024), (3, 100003)])
+def test_argmax_rows_matches_torch(cuda, dtype, rows, cols):
+    g = torch.Generator().manual_seed(rows * 31 + cols)
+    x = torch.randn(rows, cols, generator=g).to(dtype)
+    # exact ties (first index wins) and a NaN row (first NaN wins)
+    x[0, cols // 3] = 50.0
+    x[0, cols // 2] = 50.0
+    if rows > 2:
+        x[2, cols - 1] = float("nan")
+        x[2, 1] = float("nan")
+    x = x.to(cuda)
+    for _ in range(3):  # counters must be reset by every call
+        got = ops().argmax_rows(x)
+        assert torch.equal(got, x.argmax(dim=-1))
+    view = x[:, : cols - 1] if cols > 1 else x  # row stride larger than the row
+    assert torch.equal(ops().argmax_rows(view), view.argmax(dim=-1))
