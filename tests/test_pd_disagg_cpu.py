@@ -124,3 +124,51 @@ def test_prefill_decode_handoff_over_gloo(tmp_path):
     assert len(dec["tokens"]) == len(PROMPT_LENS)
     for toks in dec["tokens"].values():
         assert len(toks) == NEW_TOKENS and toks[0] == 1
+
+
+def _two_pair_worker(rank, port, result_path):
+    """Ranks 2k / 2k+1 form pair k (as bench.py --gpus 4); the router splits the requests."""
+    from test_scheduler_host import ScriptedModel
+
+    store = dist.TCPStore("127.0.0.1", port, 4, rank == 0, timeout=timedelta(seconds=60))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=4, timeout=timedelta(seconds=60))
+    prompts = _prompts()
+    work = [p.shape[1] + NEW_TOKENS for p in prompts]
+    mine = assign_pairs(work, 2)[rank // 2]
+    channel = PairChannel(store, rank, rank ^ 1, HEADER_WORDS + 16)
+    schedules = {f"pd-{i}": tuple(range(1, 8)) for i in range(len(prompts))}
+    if rank % 2 == 0:
+        cache = PagedKVCache(16, 4, 1, 1, 4, torch.float32, "cpu")
+        stats = run_prefill(ScriptedModel(schedules), cache, channel, [(i, prompts[i]) for i in mine],
+                            token_budget=24, idle_sleep=0.001)
+        result = {"mine": mine, "requests": stats.requests, "free": cache.allocator.free_block_count}
+    else:
+        cache = PagedKVCache(64, 4, 1, 1, 4, torch.float32, "cpu")
+
+        def fake_import(c, sid, length, src_blocks):
+            c.ensure_capacity(sid, length)
+            c.advance(sid, length)
+            return None
+
+        reqs = run_decode(ScriptedModel(schedules), cache, channel, lambda i: prompts[i],
+                          GenerationConfig(max_new_tokens=NEW_TOKENS), 3, fake_import, 8, idle_sleep=0.001)
+        result = {"mine": mine, "done": sorted(int(r.sequence_id[3:]) for r in reqs),
+                  "status": sorted({r.status.value for r in reqs}), "free": cache.allocator.free_block_count}
+    torch.save(result, f"{result_path}.{rank}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_pairs_split_requests_over_four_ranks(tmp_path):
+    path = str(tmp_path / "res4")
+    mp.start_processes(_two_pair_worker, args=(_free_port(), path), nprocs=4, start_method="spawn", join=True)
+    res = [torch.load(f"{path}.{r}") for r in range(4)]
+    # both pairs got work, nothing twice, nothing lost
+    assert res[0]["mine"] and res[2]["mine"]
+    assert sorted(res[0]["mine"] + res[2]["mine"]) == list(range(len(PROMPT_LENS)))
+    for pair in (0, 1):
+        pre, dec = res[2 * pair], res[2 * pair + 1]
+        assert pre["requests"] == len(pre["mine"])
+        assert dec["done"] == sorted(pre["mine"])
+        assert dec["status"] == ["completed"]
+        assert pre["free"] == 16 and dec["free"] == 64
