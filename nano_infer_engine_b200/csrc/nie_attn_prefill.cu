@@ -1,21 +1,30 @@
 // (d) Varlen causal attention over the paged cache on the 5th-generation
 // tensor cores (tcgen05 + TMEM), bf16 / head_dim 64 / block_size 16.
 //
-// One CTA computes one (128-query tile of one request, one query head); two
-// CTAs share an SM (256 TMEM columns, <= 168 registers and ~98 KiB of shared
-// memory each), so each SM sub-partition has two softmax warps in flight.
+// Work decomposition (persistent, stream-K).  A "segment" is one (128-query
+// tile of one request, query head) pair; it owns ceil(keys / 64) key tiles.
+// All segments are laid end to end (query tile major, head minor, so the
+// heads sharing a kv head are neighbours) and the resulting list of key tiles
+// is cut into equal contiguous ranges, one per CTA, with two CTAs per SM and
+// one wave: every SM does the same amount of tile work whatever the length
+// mix, and each CTA pays its prologue once.  A segment that lies wholly in
+// one CTA's range is normalised and written by that CTA; a segment cut by a
+// range boundary leaves (max, sum, unnormalised O) partials in one of two
+// slots of each CTA it touches, which prefill_combine_kernel merges in CTA
+// order.  Without a workspace each CTA takes exactly one segment instead.
 //
-//   warp 4  TMA producer   Q tile once (128 rows x 128 B), then per 64-key
-//                          tile 4+4 block loads of K and V rows of the kv head
-//                          (2 KiB each, 128-byte swizzle) into a 5-stage ring;
-//                          blocks past the needed keys are fetched out of
-//                          bounds, i.e. as zeros.
-//   warp 5  MMA issuer     one thread issues S_j = Q K_j^T (M=128, N=64,
-//                          4 x K=16, both operands from shared memory) into one
-//                          of two TMEM S buffers, and O += P_j V_j (M=128,
-//                          N=64, 4 x K=16, A = P read from TMEM, V as an
-//                          MN-major operand) into a TMEM O accumulator that
-//                          lives across all key tiles.
+// Roles of the 6 warps of a CTA (all iterate the same segments / tiles):
+//   warp 4  TMA producer   per segment the Q tile (128 rows x 128 B) into one
+//                          of two Q buffers, then per 64-key tile 4+4 block
+//                          loads of K and V rows of the kv head (2 KiB each,
+//                          128-byte swizzle) into a 4-stage ring; blocks past
+//                          the needed keys are fetched out of bounds (zeros).
+//   warp 5  MMA issuer     one thread issues S_g = Q K_g^T (M=128, N=64,
+//                          4 x K=16, operands in shared memory) into one of
+//                          two TMEM S buffers, then O += P_{g-1} V_{g-1}
+//                          (M=128, N=64, 4 x K=16, A = P read from TMEM, V as
+//                          an MN-major operand) into the segment's TMEM O
+//                          buffer (two O buffers alternate between segments).
 //   warps 0-3 softmax      thread t owns query row t: one pass over its S row
 //                          (64 values in registers): reference rounding
 //                          (score = bf16(bf16(q.k) * scale); exact as one
@@ -26,8 +35,10 @@
 //                          by more than 2^8 (lazy rescale: O in TMEM and l are
 //                          then scaled once); otherwise P is taken against the
 //                          stale max, which stays exact because the final
-//                          O / l uses the same reference.  Epilogue: O / l.
+//                          O / l uses the same reference.  Segment end: O / l
+//                          (or the partial), then the O buffer is released.
 //
+// TMEM (256 columns per CTA): S0 0-63, S1 64-127, O0 128-191, O1 192-255.
 // Waits are bounded: a wait that runs out raises NIE_DEV_ERR_TIMEOUT, the
 // CTA stops issuing work, drains what is in flight and frees its TMEM.
 #include "nie_attn.cuh"
@@ -39,16 +50,21 @@ constexpr int kPfBN = 64;
 constexpr int kPfHD = 64;
 constexpr int kPfBS = 16;
 constexpr int kPfBlocksPerTile = kPfBN / kPfBS;
-constexpr int kPfStages = 5;
+constexpr int kPfStages = 4;
 constexpr int kPfThreads = 192;
 constexpr uint32_t kPfTmemCols = 256;
 constexpr uint32_t kPfWait = 1u << 22;
-constexpr int kPfTileQ = kPfBM * kPfHD * 2;   // 16 KiB
-constexpr int kPfTileKV = kPfBN * kPfHD * 2;  // 8 KiB
+constexpr int kPfTileQ = kPfBM * kPfHD * 2;       // 16 KiB
+constexpr int kPfTileKV = kPfBN * kPfHD * 2;      // 8 KiB
 constexpr int kPfBlockBytes = kPfBS * kPfHD * 2;  // 2 KiB
-constexpr uint32_t kSCol0 = 0, kSCol1 = 64, kOCol = 128;
+constexpr uint32_t kSCol0 = 0, kSCol1 = 64, kOCol0 = 128;  // O buffer b at kOCol0 + 64 b
 constexpr float kPfLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kPfMaxUnits = 2048;  // 128-query tiles per call (larger calls use the generic kernel)
+constexpr int kPfMaxCtas = 320;    // persistent grid bound (2 per SM)
+constexpr int kPfPartialFloats = (2 + kPfHD) * kPfBM;  // m[128], l[128], O[64][128]
+// workspace: [cum: kPfMaxUnits + 2 int32 (tile prefix sums, then W) | partials]
+constexpr size_t kPfCumBytes = ((size_t)(kPfMaxUnits + 2) * sizeof(int32_t) + 255) & ~size_t(255);
 
 struct PrefillArgs {
   __nv_bfloat16* out;
@@ -62,28 +78,31 @@ struct PrefillArgs {
   const int64_t* qsl;
   const int32_t* req_list;
   int tiles_per_req;
-  int chunks;       // key chunks per query tile (grid bound); 1 = no split
-  int chunk_tiles;  // key tiles per chunk
-  float* partials;  // [grid.x][hq] x {m[128], l[128], O[64][128]} when chunks > 1
+  int units;        // num_requests * tiles_per_req query tiles
+  int stream;       // 1: equal tile ranges per CTA + partials; 0: one segment per CTA
+  float* partials;  // [grid][2] x kPfPartialFloats (stream mode)
+  int32_t* cum_out; // kPfCumBytes of the workspace (stream mode)
   float scale;
   float scale_log2e;
   int scale_pow2;
   int32_t* err;
 };
 
-constexpr int kPfChunkTiles = 16;                   // 1024 keys per CTA at most
-constexpr int kPfPartialFloats = (2 + kPfHD) * kPfBM;  // one (unit, head) partial
-
 struct PfBars {
-  uint64_t q_full;
+  uint64_t q_full[2];
+  uint64_t q_empty[2];
   uint64_t kv_full[kPfStages];
   uint64_t kv_empty[kPfStages];
   uint64_t s_full[2];
   uint64_t p_full[2];
-  uint64_t o_done;
+  uint64_t o_done;      // every P V product (global tile order)
+  uint64_t o_full[2];   // a segment's last P V product, per O buffer
+  uint64_t o_free[2];   // the softmax warps have read an O buffer
   uint64_t done;
   uint32_t tmem_base;
   int abort;
+  int red[kPfThreads];
+  int cum[kPfMaxUnits + 1];
 };
 
 // Bounded wait that also gives up once another warp aborted the CTA.
@@ -104,45 +123,152 @@ __device__ __forceinline__ void round_bf16_pair(float& a, float& b) {
   b = __high2float(h);
 }
 
+// Geometry of one 128-query tile ("unit").
+struct PfUnit {
+  int64_t qs;   // first query row of the request
+  int q0, nq;   // tile offset in the request, rows in the tile
+  int ctx;      // cached tokens before the request's queries
+  int seq_len;
+  int trow;     // block-table row
+  int n_kt;     // key tiles (0: the tile is past the request's queries)
+};
+
+__device__ __forceinline__ PfUnit pf_unit(const PrefillArgs& a, int u) {
+  PfUnit x;
+  const int item = u / a.tiles_per_req, tile = u % a.tiles_per_req;
+  const int r = a.req_list ? a.req_list[item] : item;
+  x.qs = a.qsl[r];
+  const int qlen = (int)(a.qsl[r + 1] - x.qs);
+  x.q0 = tile * kPfBM;
+  x.nq = min(kPfBM, qlen - x.q0);
+  x.seq_len = a.seq_lens[r];
+  x.ctx = x.seq_len - qlen;
+  x.trow = a.table_rows ? a.table_rows[r] : r;
+  x.n_kt = x.q0 < qlen ? (x.ctx + x.q0 + x.nq + kPfBN - 1) / kPfBN : 0;
+  return x;
+}
+
+// Walks the segments that overlap this CTA's key-tile range [lo, hi) of the
+// global list; identical in every warp.  cum[u] = key tiles of units < u.
+struct PfSegIter {
+  const int* cum;
+  int units, hq;
+  int64_t lo, hi;
+  int u, h;        // current segment
+  int64_t start;   // its first global tile
+  int n;           // its key tiles
+
+  __device__ void init(const int* c, int U, int H, int64_t a_lo, int64_t a_hi) {
+    cum = c;
+    units = U;
+    hq = H;
+    lo = a_lo;
+    hi = a_hi;
+    // largest unit with hq * cum[u] <= lo (it has tiles since lo < total)
+    int l = 0, r = U - 1;
+    while (l < r) {
+      const int m = (l + r + 1) >> 1;
+      if ((int64_t)hq * cum[m] <= lo) l = m; else r = m - 1;
+    }
+    u = l;
+    n = cum[u + 1] - cum[u];
+    h = n > 0 ? (int)((lo - (int64_t)hq * cum[u]) / n) : 0;
+    start = (int64_t)hq * cum[u] + (int64_t)h * n;
+  }
+  __device__ bool valid() const { return lo < hi && start < hi; }
+  __device__ int t_lo() const { return (int)(max(lo, start) - start); }
+  __device__ int t_hi() const { return (int)(min(hi, start + n) - start); }
+  __device__ void next() {
+    if (++h < hq) {
+      start += n;
+      return;
+    }
+    h = 0;
+    do {
+      ++u;
+    } while (u < units && cum[u + 1] == cum[u]);
+    if (u >= units) {
+      start = hi;
+      return;
+    }
+    n = cum[u + 1] - cum[u];
+    start = (int64_t)hq * cum[u];
+  }
+};
+
 __global__ void __launch_bounds__(kPfThreads, 2)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, PrefillArgs a) {
   extern __shared__ uint8_t pf_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(pf_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sq = sm;
-  uint8_t* skv = sm + kPfTileQ;
+  uint8_t* sq = sm;                     // two Q buffers
+  uint8_t* skv = sm + 2 * kPfTileQ;     // K/V ring
   PfBars* b = reinterpret_cast<PfBars*>(skv + kPfStages * 2 * kPfTileKV);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int U = a.units;
 
-  // ---- work item (uniform across the CTA, decided before any barrier)
-  const int chunk = blockIdx.x % a.chunks, unit = blockIdx.x / a.chunks;
-  const int item = unit / a.tiles_per_req, tile = unit % a.tiles_per_req;
-  const int r = a.req_list ? a.req_list[item] : item;
-  const int64_t qs = a.qsl[r];
-  const int qlen = (int)(a.qsl[r + 1] - qs);
-  const int q0 = tile * kPfBM;
-  if (q0 >= qlen) return;
-  const int nq = min(kPfBM, qlen - q0);
-  const int h = blockIdx.y, kvh = h / a.group;
-  const int seq_len = a.seq_lens[r];
-  const int ctx = seq_len - qlen;
-  const int n_keys = ctx + q0 + nq;
-  const int n_kt_all = (n_keys + kPfBN - 1) / kPfBN;
-  const int kt0 = chunk * a.chunk_tiles;  // first key tile of this CTA
-  if (kt0 >= n_kt_all) return;
-  const int n_kt = min(a.chunk_tiles, n_kt_all - kt0);  // key tiles of this CTA
-  const bool split = (n_kt_all + a.chunk_tiles - 1) / a.chunk_tiles > 1;
-  const int trow = a.table_rows ? a.table_rows[r] : r;
+  // ---- key tiles per unit and their prefix sums (the whole CTA)
+  {
+    const int per = (U + kPfThreads - 1) / kPfThreads;
+    const int u0 = threadIdx.x * per, u1 = min(U, u0 + per);
+    int local = 0;
+    for (int u = u0; u < u1; ++u) {
+      const int n = pf_unit(a, u).n_kt;
+      b->cum[u] = n;
+      local += n;
+    }
+    b->red[threadIdx.x] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int run = 0;
+      for (int i = 0; i < kPfThreads; ++i) {
+        const int v = b->red[i];
+        b->red[i] = run;
+        run += v;
+      }
+      b->cum[U] = run;
+    }
+    __syncthreads();
+    int run = b->red[threadIdx.x];
+    for (int u = u0; u < u1; ++u) {
+      const int v = b->cum[u];
+      b->cum[u] = run;
+      run += v;
+    }
+    __syncthreads();
+  }
+  const int64_t total = (int64_t)a.hq * b->cum[U];
+  int64_t lo, hi;
+  int64_t W = 0;
+  if (a.stream) {
+    W = (total + gridDim.x - 1) / gridDim.x;
+    lo = (int64_t)blockIdx.x * W;
+    hi = min(total, lo + W);
+    if (blockIdx.x == 0) {
+      for (int u = threadIdx.x; u <= U; u += kPfThreads) a.cum_out[u] = b->cum[u];
+      if (threadIdx.x == 0) a.cum_out[kPfMaxUnits + 1] = (int32_t)W;
+    }
+  } else {
+    // one segment per CTA: blockIdx.x = unit * hq + head
+    const int u = blockIdx.x / a.hq, h = blockIdx.x % a.hq;
+    const int n = b->cum[u + 1] - b->cum[u];
+    lo = (int64_t)a.hq * b->cum[u] + (int64_t)h * n;
+    hi = lo + n;
+  }
+  if (lo >= hi) return;  // uniform: nothing to do for this CTA
 
   if (threadIdx.x == 0) {
-    mbar_init(&b->q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&b->q_full[i], 1);
+      mbar_init(&b->q_empty[i], 1);
+      mbar_init(&b->s_full[i], 1);
+      mbar_init(&b->p_full[i], kPfBM);
+      mbar_init(&b->o_full[i], 1);
+      mbar_init(&b->o_free[i], kPfBM);
+    }
     for (int s = 0; s < kPfStages; ++s) {
       mbar_init(&b->kv_full[s], 1);
       mbar_init(&b->kv_empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&b->s_full[i], 1);
-      mbar_init(&b->p_full[i], kPfBM);
     }
     mbar_init(&b->o_done, 1);
     mbar_init(&b->done, 1);
@@ -157,6 +283,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = b->tmem_base;
+  PfSegIter seg;
+  seg.init(b->cum, U, a.hq, lo, hi);
 
   if (warp == 4) {
     // ------------------------------------------------------ TMA producer
@@ -164,71 +292,87 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
-      mbar_arrive_expect_tx(&b->q_full, kPfTileQ);
-      tma_load_3d(sq, &qmap, &b->q_full, 0, h, (int)(qs + q0));
     }
-    int issued = 0;
-    for (int kt = 0; kt < n_kt; ++kt) {
-      const int st = kt % kPfStages;
-      if (kt >= kPfStages && !pf_wait(b, &b->kv_empty[st], (uint32_t)((kt - kPfStages) / kPfStages) & 1u, a.err))
+    int k = 0;        // segments of this CTA so far
+    int64_t g = 0;    // key tiles of this CTA so far
+    int64_t issued = 0;
+    int q_issued = 0;
+    bool ok = true;
+    for (; ok && seg.valid(); seg.next(), ++k) {
+      const PfUnit x = pf_unit(a, seg.u);
+      const int qb = k & 1;
+      if (k >= 2 && !pf_wait(b, &b->q_empty[qb], (uint32_t)((k - 2) >> 1) & 1u, a.err)) {
+        ok = false;
         break;
-      int coord = (int)(a.nb * kPfBS);  // out of bounds: zero fill
-      if (lane < kPfBlocksPerTile) {
-        const int lb = (kt0 + kt) * kPfBlocksPerTile + lane;
-        if (lb * kPfBS < n_keys) {
-          int64_t blk = (lb < a.tstride) ? (int64_t)a.tables[(int64_t)trow * a.tstride + lb] : -1;
-          if (blk < 0 || blk >= a.nb) {
-            raise_flag(a.err, NIE_DEV_ERR_BLOCK_RANGE);
-            blk = 0;
-          }
-          coord = (int)(blk * kPfBS);
+      }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&b->q_full[qb], kPfTileQ);
+        tma_load_3d(sq + qb * kPfTileQ, &qmap, &b->q_full[qb], 0, seg.h, (int)(x.qs + x.q0));
+      }
+      q_issued = k + 1;
+      const int kvh = seg.h / a.group;
+      const int n_keys = x.ctx + x.q0 + x.nq;
+      for (int kt = seg.t_lo(); kt < seg.t_hi(); ++kt, ++g) {
+        const int st = (int)(g % kPfStages);
+        if (g >= kPfStages && !pf_wait(b, &b->kv_empty[st], (uint32_t)((g - kPfStages) / kPfStages) & 1u, a.err)) {
+          ok = false;
+          break;
         }
+        int coord = (int)(a.nb * kPfBS);  // out of bounds: zero fill
+        if (lane < kPfBlocksPerTile) {
+          const int lb = kt * kPfBlocksPerTile + lane;
+          if (lb * kPfBS < n_keys) {
+            int64_t blk = (lb < a.tstride) ? (int64_t)a.tables[(int64_t)x.trow * a.tstride + lb] : -1;
+            if (blk < 0 || blk >= a.nb) {
+              raise_flag(a.err, NIE_DEV_ERR_BLOCK_RANGE);
+              blk = 0;
+            }
+            coord = (int)(blk * kPfBS);
+          }
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&b->kv_full[st], 2 * kPfTileKV);
+        __syncwarp();
+        if (lane < kPfBlocksPerTile) {
+          uint8_t* dst = skv + st * 2 * kPfTileKV + lane * kPfBlockBytes;
+          tma_load_3d(dst, &kmap, &b->kv_full[st], 0, kvh, coord);
+          tma_load_3d(dst + kPfTileKV, &vmap, &b->kv_full[st], 0, kvh, coord);
+        }
+        issued = g + 1;
       }
-      if (lane == 0) mbar_arrive_expect_tx(&b->kv_full[st], 2 * kPfTileKV);
-      __syncwarp();
-      if (lane < kPfBlocksPerTile) {
-        uint8_t* dst = skv + st * 2 * kPfTileKV + lane * kPfBlockBytes;
-        tma_load_3d(dst, &kmap, &b->kv_full[st], 0, kvh, coord);
-        tma_load_3d(dst + kPfTileKV, &vmap, &b->kv_full[st], 0, kvh, coord);
-      }
-      issued = kt + 1;
     }
     if (*reinterpret_cast<volatile int*>(&b->abort)) {
       // drain copies still in flight before the CTA exits
-      mbar_wait_bounded(&b->q_full, 0, kPfWait);
-      for (int kt = max(0, issued - kPfStages); kt < issued; ++kt)
-        mbar_wait_bounded(&b->kv_full[kt % kPfStages], (uint32_t)(kt / kPfStages) & 1u, kPfWait);
+      for (int kq = max(0, q_issued - 2); kq < q_issued; ++kq)
+        mbar_wait_bounded(&b->q_full[kq & 1], (uint32_t)(kq >> 1) & 1u, kPfWait);
+      for (int64_t gg = max((int64_t)0, issued - kPfStages); gg < issued; ++gg)
+        mbar_wait_bounded(&b->kv_full[gg % kPfStages], (uint32_t)(gg / kPfStages) & 1u, kPfWait);
     }
   } else if (warp == 5) {
     // ------------------------------------------------------- MMA issuer
     const uint32_t id_s = idesc_bf16_f32(kPfBM, kPfBN, false, false);
     const uint32_t id_pv = idesc_bf16_f32(kPfBM, kPfHD, false, true);
-    const uint32_t q_addr = smem_u32(sq);
-    const int last_lb = (seq_len - 1) / kPfBS;
-    const int tail = seq_len % kPfBS;
-    bool ok = pf_wait(b, &b->q_full, 0, a.err);
+    bool ok = true;
+    // the P V product still to issue (one tile behind S)
+    struct Pend {
+      bool live = false;
+      int64_t g;
+      int ob;           // O buffer of its segment
+      int k;            // its segment's index in this CTA
+      bool first, last; // first / last tile of that segment in this CTA
+      int seq_len;      // its sequence: stale V rows past the end are zeroed
+      int kt;           // its key tile index within the segment
+    } pend;
 
-    auto issue_s = [&](int j) -> bool {
-      const int st = j % kPfStages;
-      if (!pf_wait(b, &b->kv_full[st], (uint32_t)(j / kPfStages) & 1u, a.err)) return false;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t k_addr = smem_u32(skv + st * 2 * kPfTileKV);
-        const uint32_t d = tbase + ((j & 1) ? kSCol1 : kSCol0);
-#pragma unroll
-        for (int k = 0; k < kPfHD / 16; ++k)
-          tc_mma_ss(d, smem_desc_sw128(q_addr + k * 32, 16, 1024), smem_desc_sw128(k_addr + k * 32, 16, 1024), id_s,
-                    k > 0 ? 1u : 0u);
-        tc_commit(&b->s_full[j & 1]);
-      }
-      __syncwarp();
-      return true;
-    };
-    auto issue_pv = [&](int j) -> bool {
-      if (!pf_wait(b, &b->p_full[j & 1], (uint32_t)(j >> 1) & 1u, a.err)) return false;
-      const int st = j % kPfStages;
+    auto issue_pv = [&](const Pend& p) -> bool {
+      if (!pf_wait(b, &b->p_full[p.g & 1], (uint32_t)(p.g >> 1) & 1u, a.err)) return false;
+      if (p.first && p.k >= 2 &&
+          !pf_wait(b, &b->o_free[p.ob], (uint32_t)((p.k - 2) >> 1) & 1u, a.err))
+        return false;  // the softmax warps still read this O buffer's previous segment
+      const int st = (int)(p.g % kPfStages);
       uint8_t* vt = skv + st * 2 * kPfTileKV + kPfTileKV;
-      if (tail != 0 && last_lb / kPfBlocksPerTile == kt0 + j && last_lb * kPfBS < n_keys) {
+      const int last_lb = (p.seq_len - 1) / kPfBS;
+      const int tail = p.seq_len % kPfBS;
+      if (tail != 0 && last_lb / kPfBlocksPerTile == p.kt) {
         // stale rows past the sequence end (possibly NaN) must not meet P = 0
         uint4* z = reinterpret_cast<uint4*>(vt + (last_lb % kPfBlocksPerTile) * kPfBlockBytes + tail * (kPfHD * 2));
         for (int c = lane; c < (kPfBS - tail) * 8; c += 32) z[c] = make_uint4(0u, 0u, 0u, 0u);
@@ -238,24 +382,62 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       tc_fence_after();
       if (lane == 0) {
         const uint32_t v_addr = smem_u32(vt);
-        const uint32_t p = tbase + ((j & 1) ? kSCol1 : kSCol0);
+        const uint32_t pcol = tbase + ((p.g & 1) ? kSCol1 : kSCol0);
+        const uint32_t ocol = tbase + kOCol0 + 64u * (uint32_t)p.ob;
 #pragma unroll
-        for (int k = 0; k < kPfBN / 16; ++k)
-          tc_mma_ts(tbase + kOCol, p + k * 8, smem_desc_sw128(v_addr + k * 2048, kPfTileKV, 1024), id_pv,
-                    (j > 0 || k > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kPfBN / 16; ++kk)
+          tc_mma_ts(ocol, pcol + kk * 8, smem_desc_sw128(v_addr + kk * 2048, kPfTileKV, 1024), id_pv,
+                    (!p.first || kk > 0) ? 1u : 0u);
         tc_commit(&b->o_done);
         tc_commit(&b->kv_empty[st]);
+        if (p.last) tc_commit(&b->o_full[p.ob]);
       }
       __syncwarp();
       return true;
     };
 
-    if (ok && n_kt > 0) ok = issue_s(0);
-    for (int j = 1; ok && j < n_kt; ++j) {
-      ok = issue_s(j);
-      if (ok) ok = issue_pv(j - 1);
+    int k = 0;
+    int64_t g = 0;
+    for (; ok && seg.valid(); seg.next(), ++k) {
+      const PfUnit x = pf_unit(a, seg.u);
+      const int qb = k & 1;
+      if (!pf_wait(b, &b->q_full[qb], (uint32_t)(k >> 1) & 1u, a.err)) {
+        ok = false;
+        break;
+      }
+      const uint32_t q_addr = smem_u32(sq + qb * kPfTileQ);
+      const int tlo = seg.t_lo(), thi = seg.t_hi();
+      for (int kt = tlo; ok && kt < thi; ++kt, ++g) {
+        const int st = (int)(g % kPfStages);
+        if (!pf_wait(b, &b->kv_full[st], (uint32_t)(g / kPfStages) & 1u, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t k_addr = smem_u32(skv + st * 2 * kPfTileKV);
+          const uint32_t d = tbase + ((g & 1) ? kSCol1 : kSCol0);
+#pragma unroll
+          for (int kk = 0; kk < kPfHD / 16; ++kk)
+            tc_mma_ss(d, smem_desc_sw128(q_addr + kk * 32, 16, 1024), smem_desc_sw128(k_addr + kk * 32, 16, 1024),
+                      id_s, kk > 0 ? 1u : 0u);
+          tc_commit(&b->s_full[g & 1]);
+          // the Q buffer is free once this segment's last S product completes
+          if (kt + 1 == thi) tc_commit(&b->q_empty[qb]);
+        }
+        __syncwarp();
+        if (pend.live) ok = issue_pv(pend);
+        pend.live = true;
+        pend.g = g;
+        pend.ob = k & 1;
+        pend.k = k;
+        pend.first = kt == tlo;
+        pend.last = kt + 1 == thi;
+        pend.seq_len = x.seq_len;
+        pend.kt = kt;
+      }
     }
-    if (ok && n_kt > 0) issue_pv(n_kt - 1);
+    if (ok && pend.live) issue_pv(pend);
     if (lane == 0) tc_commit(&b->done);
     __syncwarp();
     mbar_wait_bounded(&b->done, 0, kPfWait);
@@ -263,127 +445,141 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     // -------------------------------------------------- softmax warps
     const int t = threadIdx.x;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    const int qpos = ctx + q0 + t;
-    const int diag_from = ctx + q0;  // smallest query position of the tile
-    float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     uint32_t v[64];
-
-    for (int j = 0; j < n_kt; ++j) {
-      const int sb = j & 1;
-      if (!pf_wait(b, &b->s_full[sb], (uint32_t)(j >> 1) & 1u, a.err)) {
+    int k = 0;
+    int64_t g = 0;
+    for (; ok && seg.valid(); seg.next(), ++k) {
+      const PfUnit x = pf_unit(a, seg.u);
+      const int ob = k & 1;
+      const uint32_t ocol = kOCol0 + 64u * (uint32_t)ob;
+      const int qpos = x.ctx + x.q0 + t;
+      const int diag_from = x.ctx + x.q0;  // smallest query position of the tile
+      const int tlo = seg.t_lo(), thi = seg.t_hi();
+      float m_ref = -INFINITY, l = 0.f;
+      for (int kt = tlo; kt < thi; ++kt, ++g) {
+        const int sb = (int)(g & 1);
+        if (!pf_wait(b, &b->s_full[sb], (uint32_t)(g >> 1) & 1u, a.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t s_addr = tbase + lane_off + (sb ? kSCol1 : kSCol0);
+        tmem_ld32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
+        const int key0 = kt * kPfBN;
+        const bool masked = key0 + kPfBN - 1 > diag_from;
+        // v holds the rounded scores in the "raw" domain (before * scale*log2e,
+        // a positive factor, so the max can be taken before scaling); eight
+        // independent max chains
+        float mxa[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mxa[i] = -INFINITY;
+        if (a.scale_pow2) {
+          // bf16(bf16(acc) * 2^k) == bf16(acc) * 2^k: one rounding
+#pragma unroll
+          for (int e = 0; e < 64; e += 2) {
+            float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
+            round_bf16_pair(x0, x1);
+            if (masked) {
+              if (key0 + e > qpos) x0 = -INFINITY;
+              if (key0 + e + 1 > qpos) x1 = -INFINITY;
+            }
+            v[e] = __float_as_uint(x0);
+            v[e + 1] = __float_as_uint(x1);
+            mxa[(e >> 1) & 7] = fmaxf(mxa[(e >> 1) & 7], fmaxf(x0, x1));
+          }
+        } else {
+          // bf16(bf16(acc) * scale), kept in the raw domain
+#pragma unroll
+          for (int e = 0; e < 64; e += 2) {
+            float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
+            round_bf16_pair(x0, x1);
+            x0 *= a.scale;
+            x1 *= a.scale;
+            round_bf16_pair(x0, x1);
+            x0 /= a.scale;  // exact: undoes a multiply whose result is representable
+            x1 /= a.scale;
+            if (masked) {
+              if (key0 + e > qpos) x0 = -INFINITY;
+              if (key0 + e + 1 > qpos) x1 = -INFINITY;
+            }
+            v[e] = __float_as_uint(x0);
+            v[e + 1] = __float_as_uint(x1);
+            mxa[(e >> 1) & 7] = fmaxf(mxa[(e >> 1) & 7], fmaxf(x0, x1));
+          }
+        }
+        const float mx_raw = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                                   fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+        const float mx = mx_raw * a.scale_log2e;
+        const bool raise = mx > m_ref + kRescaleLog2;
+        if (__any_sync(0xffffffffu, raise)) {
+          const float alpha = raise ? fast_exp2(m_ref - mx) : 1.f;
+          if (raise) {
+            l *= alpha;
+            m_ref = mx;
+          }
+          if (kt > tlo) {
+            // O must hold P_{g-1} V_{g-1} (this segment's previous tile) before
+            // it is rescaled.  S_g was issued after P_{g-2} V_{g-2} and its
+            // commit covers every earlier MMA, so o_done has completed g-1 or g
+            // phases here: the parity wait for phase g-1 is unambiguous
+            // although earlier phases were not waited on.
+            if (!pf_wait(b, &b->o_done, (uint32_t)(g - 1) & 1u, a.err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            uint32_t o[32];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              tmem_ld32(tbase + lane_off + ocol + 32 * half, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+              tmem_st32(tbase + lane_off + ocol + 32 * half, o);
+            }
+          }
+        }
+        float rsa[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rsa[i] = 0.f;
+        uint32_t pk[32];
+        // a row whose keys in this range are all masked keeps m_ref = -inf:
+        // its p must come out 0, not exp2(-inf + inf)
+        const float sl2e = a.scale_log2e, neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(v[2 * e]), sl2e, neg_m));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(v[2 * e + 1]), sl2e, neg_m));
+          rsa[e & 7] += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        const float rs = ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3])) + ((rsa[4] + rsa[5]) + (rsa[6] + rsa[7]));
+        tmem_st32(s_addr, pk);
+        tmem_wait_st();
+        l += rs;
+        tc_fence_before();
+        mbar_arrive(&b->p_full[sb]);
+      }
+      if (!ok) break;
+      // the segment's last P V product has completed once o_full fires (one
+      // phase per use of the buffer)
+      if (!pf_wait(b, &b->o_full[ob], (uint32_t)(k >> 1) & 1u, a.err)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t s_addr = tbase + lane_off + (sb ? kSCol1 : kSCol0);
-      tmem_ld32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-      tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_ld32(tbase + lane_off + ocol, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_ld32(tbase + lane_off + ocol + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
       tmem_wait_ld();
-      const int key0 = (kt0 + j) * kPfBN;
-      const bool masked = key0 + kPfBN - 1 > diag_from;
-      // v holds the rounded scores in the "raw" domain (before * scale*log2e,
-      // a positive factor, so the max can be taken before scaling)
-      // eight independent max chains (a single chain is 32 dependent ops)
-      float mxa[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mxa[i] = -INFINITY;
-      if (a.scale_pow2) {
-        // bf16(bf16(acc) * 2^k) == bf16(acc) * 2^k: one rounding
-#pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
-          round_bf16_pair(x0, x1);
-          if (masked) {
-            if (key0 + e > qpos) x0 = -INFINITY;
-            if (key0 + e + 1 > qpos) x1 = -INFINITY;
-          }
-          v[e] = __float_as_uint(x0);
-          v[e + 1] = __float_as_uint(x1);
-          mxa[(e >> 1) & 7] = fmaxf(mxa[(e >> 1) & 7], fmaxf(x0, x1));
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
-          round_bf16_pair(x0, x1);
-          x0 *= a.scale;
-          x1 *= a.scale;
-          round_bf16_pair(x0, x1);
-          x0 /= a.scale;  // exact: undoes a multiply whose result is representable
-          x1 /= a.scale;
-          if (masked) {
-            if (key0 + e > qpos) x0 = -INFINITY;
-            if (key0 + e + 1 > qpos) x1 = -INFINITY;
-          }
-          v[e] = __float_as_uint(x0);
-          v[e + 1] = __float_as_uint(x1);
-          mxa[(e >> 1) & 7] = fmaxf(mxa[(e >> 1) & 7], fmaxf(x0, x1));
-        }
-      }
-      const float mx_raw = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                                 fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-      const float mx = mx_raw * a.scale_log2e;
-      const bool raise = mx > m_ref + kRescaleLog2;
-      if (__any_sync(0xffffffffu, raise)) {
-        const float alpha = raise ? fast_exp2(m_ref - mx) : 1.f;
-        if (raise) {
-          l *= alpha;
-          m_ref = mx;
-        }
-        if (j >= 1) {
-          // O must hold P_{j-1} V_{j-1} before it is rescaled.  S_j was issued
-          // after P_{j-2} V_{j-2} and its commit covers every earlier MMA, so
-          // o_done has completed j-1 or j phases here: the parity wait for
-          // phase j-1 is unambiguous although earlier phases were not waited on.
-          if (!pf_wait(b, &b->o_done, (uint32_t)(j - 1) & 1u, a.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          uint32_t o[32];
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            tmem_ld32(tbase + lane_off + kOCol + 32 * half, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st32(tbase + lane_off + kOCol + 32 * half, o);
-          }
-        }
-      }
-      float rsa[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) rsa[i] = 0.f;
-      uint32_t pk[32];
-      // a row whose keys in this chunk are all masked keeps m_ref = -inf: its
-      // p must come out 0, not exp2(-inf + inf)
-      const float sl2e = a.scale_log2e, neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float p0 = fast_exp2(fmaf(__uint_as_float(v[2 * e]), sl2e, neg_m));
-        const float p1 = fast_exp2(fmaf(__uint_as_float(v[2 * e + 1]), sl2e, neg_m));
-        rsa[e & 7] += p0 + p1;
-        pk[e] = pack_bf16x2(p0, p1);
-      }
-      const float rs = ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3])) + ((rsa[4] + rsa[5]) + (rsa[6] + rsa[7]));
-      tmem_st32(s_addr, pk);
-      tmem_wait_st();
-      l += rs;
       tc_fence_before();
-      mbar_arrive(&b->p_full[sb]);
-    }
-    // every MMA of the CTA has completed once `done` fires (its single phase is
-    // unambiguous; o_done may be any number of phases behind the last tile)
-    if (ok && n_kt > 0) ok = pf_wait(b, &b->done, 0u, a.err);
-    if (ok) {
-      tc_fence_after();
-      tmem_ld32(tbase + lane_off + kOCol, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-      tmem_ld32(tbase + lane_off + kOCol + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-      tmem_wait_ld();
-      if (t < nq && !split) {
+      mbar_arrive(&b->o_free[ob]);
+      const bool whole = tlo == 0 && thi == seg.n;
+      if (t < x.nq && whole) {
         const float inv = 1.f / l;
-        __nv_bfloat16* op = a.out + (qs + q0 + t) * a.out_stride + (int64_t)h * kPfHD;
+        __nv_bfloat16* op = a.out + (x.qs + x.q0 + t) * a.out_stride + (int64_t)seg.h * kPfHD;
 #pragma unroll
         for (int c = 0; c < kPfHD / 8; ++c) {
           uint4 w;
@@ -393,10 +589,11 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           w.w = pack_bf16x2(__uint_as_float(v[8 * c + 6]) * inv, __uint_as_float(v[8 * c + 7]) * inv);
           *reinterpret_cast<uint4*>(op + 8 * c) = w;
         }
-      } else if (t < nq) {
-        // partial of this key chunk: m, l, unnormalised O (d-major so that a
-        // warp's stores and the combine kernel's loads are contiguous)
-        float* ps = a.partials + ((int64_t)blockIdx.x * a.hq + h) * kPfPartialFloats;
+      } else if (t < x.nq) {
+        // partial of a segment cut by this CTA's range: slot 0 = the CTA's
+        // first segment, 1 = its last (d-major so that a warp's stores and the
+        // combine kernel's loads are contiguous)
+        float* ps = a.partials + ((int64_t)blockIdx.x * 2 + (k == 0 ? 0 : 1)) * kPfPartialFloats;
         ps[t] = m_ref;
         ps[kPfBM + t] = l;
 #pragma unroll
@@ -413,29 +610,30 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   }
 }
 
-// Merge the key-chunk partials of query tiles that were split across CTAs.
+// Merge the partials of segments that were cut across CTAs (stream mode).
 // grid = (units, q_heads), one thread per query row.
 __global__ void __launch_bounds__(kPfBM) prefill_combine_kernel(PrefillArgs a) {
-  const int unit = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
-  const int item = unit / a.tiles_per_req, tile = unit % a.tiles_per_req;
-  const int r = a.req_list ? a.req_list[item] : item;
-  const int64_t qs = a.qsl[r];
-  const int qlen = (int)(a.qsl[r + 1] - qs);
-  const int q0 = tile * kPfBM;
-  if (q0 >= qlen) return;
-  const int nq = min(kPfBM, qlen - q0);
-  const int ctx = a.seq_lens[r] - qlen;
-  const int n_kt_all = (ctx + q0 + nq + kPfBN - 1) / kPfBN;
-  const int n_chunks = (n_kt_all + a.chunk_tiles - 1) / a.chunk_tiles;
-  if (n_chunks <= 1 || t >= nq) return;
-  auto slot = [&](int c) { return a.partials + ((int64_t)(unit * a.chunks + c) * a.hq + h) * kPfPartialFloats; };
+  const int u = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+  const int32_t* cum = a.cum_out;
+  const int n = cum[u + 1] - cum[u];
+  const int64_t W = cum[kPfMaxUnits + 1];
+  if (n == 0 || W <= 0) return;
+  const int64_t s0 = (int64_t)a.hq * cum[u] + (int64_t)h * n, s1 = s0 + n;
+  const int64_t c0 = s0 / W, c1 = (s1 - 1) / W;
+  if (c0 == c1) return;  // written directly by its CTA
+  const PfUnit x = pf_unit(a, u);
+  if (t >= x.nq) return;
+  // the partial of CTA c is in its slot 0 when the segment is c's first one
+  auto slot = [&](int64_t c) {
+    return a.partials + (c * 2 + (s0 <= c * W ? 0 : 1)) * kPfPartialFloats;
+  };
   float M = -INFINITY;
-  for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, slot(c)[t]);
+  for (int64_t c = c0; c <= c1; ++c) M = fmaxf(M, slot(c)[t]);
   float L = 0.f;
   float o[kPfHD];
 #pragma unroll
   for (int d = 0; d < kPfHD; ++d) o[d] = 0.f;
-  for (int c = 0; c < n_chunks; ++c) {
+  for (int64_t c = c0; c <= c1; ++c) {
     const float* ps = slot(c);
     const float m = ps[t];
     const float w = (m == -INFINITY) ? 0.f : fast_exp2(m - M);
@@ -444,7 +642,7 @@ __global__ void __launch_bounds__(kPfBM) prefill_combine_kernel(PrefillArgs a) {
     for (int d = 0; d < kPfHD; ++d) o[d] += ps[2 * kPfBM + d * kPfBM + t] * w;
   }
   const float inv = 1.f / L;
-  __nv_bfloat16* op = a.out + (qs + q0 + t) * a.out_stride + (int64_t)h * kPfHD;
+  __nv_bfloat16* op = a.out + (x.qs + x.q0 + t) * a.out_stride + (int64_t)h * kPfHD;
 #pragma unroll
   for (int c = 0; c < kPfHD / 8; ++c) {
     uint4 w;
@@ -456,22 +654,15 @@ __global__ void __launch_bounds__(kPfBM) prefill_combine_kernel(PrefillArgs a) {
   }
 }
 
-// Key chunks per 128-query tile for sequences of at most max_seq_len tokens.
-static int prefill_chunks(int32_t max_seq_len) {
-  if (max_seq_len <= 0) return 1;
-  const int tiles = (max_seq_len + kPfBN - 1) / kPfBN;
-  return max(1, (tiles + kPfChunkTiles - 1) / kPfChunkTiles);
-}
-
 size_t prefill_workspace_bytes(int32_t num_requests, int32_t max_query_len, int32_t max_seq_len, int32_t q_heads) {
-  const int chunks = prefill_chunks(max_seq_len);
-  if (chunks <= 1 || num_requests <= 0 || max_query_len <= 0) return 0;
-  const int64_t units = (int64_t)num_requests * ((max_query_len + kPfBM - 1) / kPfBM);
-  return (size_t)(units * chunks * q_heads) * kPfPartialFloats * sizeof(float);
+  (void)max_seq_len;
+  (void)q_heads;
+  if (num_requests <= 0 || max_query_len <= 0) return 0;
+  return kPfCumBytes + (size_t)kPfMaxCtas * 2 * kPfPartialFloats * sizeof(float);
 }
 
 static size_t prefill_smem_bytes() {
-  return 1024 + kPfTileQ + (size_t)kPfStages * 2 * kPfTileKV + sizeof(PfBars);
+  return 1024 + 2 * kPfTileQ + (size_t)kPfStages * 2 * kPfTileKV + sizeof(PfBars);
 }
 
 static bool is_pow2_float(float x) {
@@ -488,10 +679,13 @@ int launch_prefill_tc(const void* q, void* out, int64_t row_stride, int64_t num_
                       const int32_t* seq_lens, const int64_t* qsl, const int32_t* req_list, int32_t num_requests,
                       int32_t max_query_len, int32_t max_seq_len, float scale, void* workspace,
                       size_t workspace_bytes, int32_t* err_flag, cudaStream_t s) {
+  (void)max_seq_len;
+  const int tiles_per_req = (max_query_len + kPfBM - 1) / kPfBM;
+  const int64_t units = (int64_t)num_requests * tiles_per_req;
   if (num_blocks * kPfBS >= (int64_t(1) << 31) || num_q_rows >= (int64_t(1) << 31) || (row_stride % 8) != 0 ||
       (reinterpret_cast<uintptr_t>(q) % 16) != 0 || (reinterpret_cast<uintptr_t>(out) % 16) != 0 ||
       (reinterpret_cast<uintptr_t>(key_cache) % 16) != 0 || (reinterpret_cast<uintptr_t>(value_cache) % 16) != 0 ||
-      q_heads > 65535 || num_q_rows <= 0)
+      q_heads > 65535 || num_q_rows <= 0 || units <= 0 || units > kPfMaxUnits || units * q_heads >= (int64_t(1) << 31))
     return NIE_ERR_UNSUPPORTED;
   const int64_t row_bytes = (int64_t)kv_heads * kPfHD * 2;
   const int64_t layer_bytes = num_blocks * kPfBS * row_bytes;
@@ -529,21 +723,13 @@ int launch_prefill_tc(const void* q, void* out, int64_t row_stride, int64_t num_
   pa.seq_lens = seq_lens;
   pa.qsl = qsl;
   pa.req_list = req_list;
-  pa.tiles_per_req = (max_query_len + kPfBM - 1) / kPfBM;
-  pa.chunks = prefill_chunks(max_seq_len);
-  pa.chunk_tiles = kPfChunkTiles;
-  pa.partials = nullptr;
-  if (pa.chunks > 1) {
-    const size_t need = prefill_workspace_bytes(num_requests, max_query_len, max_seq_len, q_heads);
-    if (workspace != nullptr && workspace_bytes >= need && (reinterpret_cast<uintptr_t>(workspace) % 16) == 0) {
-      pa.partials = (float*)workspace;
-    } else {
-      // no scratch: one CTA per query tile walks all of its keys
-      pa.chunks = 1;
-      pa.chunk_tiles = 1 << 30;
-    }
-  } else {
-    pa.chunk_tiles = 1 << 30;
+  pa.tiles_per_req = tiles_per_req;
+  pa.units = (int)units;
+  const size_t need = prefill_workspace_bytes(num_requests, max_query_len, max_seq_len, q_heads);
+  pa.stream = workspace != nullptr && workspace_bytes >= need && (reinterpret_cast<uintptr_t>(workspace) % 256) == 0;
+  if (pa.stream) {
+    pa.cum_out = (int32_t*)workspace;
+    pa.partials = (float*)((char*)workspace + kPfCumBytes);
   }
   pa.scale = scale;
   pa.scale_log2e = scale * kPfLog2e;
@@ -556,13 +742,17 @@ int launch_prefill_tc(const void* q, void* out, int64_t row_stride, int64_t num_
     if (e != cudaSuccess) return fail(NIE_ERR_CUDA, "prefill smem %zu: %s", smem, cudaGetErrorString(e));
     s_attr = true;
   }
-  const int64_t units = (int64_t)num_requests * pa.tiles_per_req;
-  const int64_t gx = units * pa.chunks;
-  if (gx >= (int64_t(1) << 31)) return NIE_ERR_UNSUPPORTED;
-  dim3 grid((unsigned)gx, (unsigned)q_heads);
+  int grid;
+  if (pa.stream) {
+    const int sms = sm_count(stream_device(s));
+    if (sms <= 0) return fail(NIE_ERR_CUDA, "cannot query the SM count");
+    grid = std::min(2 * sms, kPfMaxCtas);
+  } else {
+    grid = (int)(units * q_heads);  // one segment per CTA
+  }
   prefill_tc_kernel<<<grid, kPfThreads, smem, s>>>(qmap, kmap, vmap, pa);
   int rc = check_launch("prefill_tc_kernel");
-  if (rc != NIE_OK || pa.chunks <= 1) return rc;
+  if (rc != NIE_OK || !pa.stream) return rc;
   prefill_combine_kernel<<<dim3((unsigned)units, (unsigned)q_heads), kPfBM, 0, s>>>(pa);
   return check_launch("prefill_combine_kernel");
 }
