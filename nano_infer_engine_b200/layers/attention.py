@@ -19,18 +19,32 @@ from .rope import Rope
 
 
 def fused_weight(module: nn.Module, names: tuple[str, ...], attr: str) -> torch.Tensor | None:
-    """The concatenated weight of ``names`` if their parameters are still views of it."""
-    buf = module.__dict__.get(attr)
+    """The concatenated weight of ``names`` if their parameters are still views of it.
+
+    Reads the module dictionaries directly: this runs for every layer of every
+    step, and nn.Module attribute lookups cost more than the check itself."""
+    d = module.__dict__
+    buf = d.get(attr)
     if buf is None:
         return None
     at = buf.data_ptr()
     step = buf.element_size()
+    mods = d["_modules"]
     for name in names:
-        w = getattr(module, name).weight
+        w = mods[name]._parameters["weight"]
         if w.data_ptr() != at or w.dtype != buf.dtype:
             return None
         at += w.numel() * step
     return buf
+
+
+def apply_linear(module: nn.Linear, x: torch.Tensor) -> torch.Tensor:
+    """``module(x)`` without nn.Module call overhead when no hook is registered."""
+    if (module._forward_hooks or module._forward_pre_hooks or nn.modules.module._global_forward_hooks
+            or nn.modules.module._global_forward_pre_hooks):
+        return module(x)
+    params = module._parameters
+    return torch.nn.functional.linear(x, params["weight"], params["bias"])
 
 
 def fuse_linears(module: nn.Module, names: tuple[str, ...], attr: str) -> bool:
@@ -152,7 +166,7 @@ class GroupedQueryAttention(nn.Module):
                 num_requests=meta.num_prefill,
                 max_seq_len=meta.max_seq_len,
             )
-        return self.o_proj(out.view(T, self.hidden_size))
+        return apply_linear(self.o_proj, out.view(T, self.hidden_size))
 
     # ---------------------------------------------------- reference entry
     def forward(

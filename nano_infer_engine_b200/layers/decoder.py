@@ -7,7 +7,7 @@ from torch import nn
 
 from .. import ops
 from ..paged_cache import PagedKVCache
-from .attention import GroupedQueryAttention, fuse_linears, fused_weight
+from .attention import GroupedQueryAttention, apply_linear, fuse_linears, fused_weight
 from .mlp import SwiGLUMLP
 from .rms_norm import RmsNorm
 
@@ -51,7 +51,7 @@ class Llama3Decoder(nn.Module):
         else:
             gate = self.ffn.gate_proj(normed2)
             up = self.ffn.up_proj(normed2)
-        return self.ffn.down_proj(ops.silu_mul(gate, up)), h
+        return apply_linear(self.ffn.down_proj, ops.silu_mul(gate, up)), h
 
     def fuse_projections(self) -> bool:
         """Single-buffer q/k/v and gate/up weights (see ``fuse_linears``)."""

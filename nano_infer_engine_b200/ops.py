@@ -42,7 +42,7 @@ def dtype_code(dtype: torch.dtype) -> int:
 
 def _require_cuda(*tensors: torch.Tensor) -> None:
     for t in tensors:
-        if t is not None and t.device.type != "cuda":
+        if t is not None and not t.is_cuda:
             raise RuntimeError(
                 "nano_infer_engine_b200 kernels require CUDA tensors "
                 f"(got a tensor on {t.device})"
@@ -53,7 +53,16 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
-def _stream(device: torch.device) -> int:
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream(where: torch.device | torch.Tensor) -> int:
+    """Handle of the current CUDA stream (the launch stream) of a device or of a tensor's device."""
+    if _raw_stream is not None:
+        if isinstance(where, torch.Tensor):
+            return _raw_stream(where.get_device())
+        return _raw_stream(where.index if where.index is not None else torch.cuda.current_device())
+    device = where.device if isinstance(where, torch.Tensor) else where
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -609,7 +618,7 @@ def add_rmsnorm(
         dtype_code(x.dtype),
         _ptr(total),
         out.data_ptr(),
-        _stream(x.device),
+        _stream(x),
     )
     check(status, "nie_add_rmsnorm")
     _count()
@@ -664,7 +673,7 @@ def rope_write_kv(
         bs,
         slot_mapping.data_ptr(),
         error_flag(q.device).data_ptr(),
-        _stream(q.device),
+        _stream(q),
     )
     check(status, "nie_rope_write_kv")
     _count()
@@ -686,7 +695,7 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
         gate.shape[0],
         gate.shape[1],
         dtype_code(gate.dtype),
-        _stream(gate.device),
+        _stream(gate),
     )
     check(status, "nie_silu_mul")
     _count()
@@ -712,7 +721,7 @@ def embed_rows(ids: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
         dtype_code(table.dtype),
         out.data_ptr(),
         error_flag(table.device).data_ptr(),
-        _stream(table.device),
+        _stream(table),
     )
     check(status, "nie_embed_rows")
     _count()
@@ -753,7 +762,7 @@ def argmax_rows(logits: torch.Tensor) -> torch.Tensor:
         out.data_ptr(),
         ws.data_ptr(),
         ws.numel(),
-        _stream(logits.device),
+        _stream(logits),
     )
     check(status, "nie_argmax_rows")
     _count()
