@@ -98,7 +98,64 @@ def build(force: bool = False, verbose: bool = False, extra_flags: tuple[str, ..
     return LIB_PATH
 
 
+EXT_SOURCE = CSRC / "nie_torch_ext.cpp"
+EXT_NAME = "_nie_torch_ext"
+EXT_PATH = PKG_DIR / (EXT_NAME + ".so")
+
+
+def build_ext(force: bool = False, verbose: bool = False) -> Path:
+    """Compile the torch C++ extension (the per-layer loop of a ragged step) with g++.
+
+    It links against ``libnie_b200.so`` beside it (rpath ``$ORIGIN``) and
+    against the installed torch, so it must be rebuilt with torch.
+    """
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension
+
+    inputs = [EXT_SOURCE, LIB_PATH, *INCLUDE_DIR.glob("*.h"), Path(torch.__file__)]
+    if not force and EXT_PATH.exists() and all(p.stat().st_mtime <= EXT_PATH.stat().st_mtime for p in inputs):
+        return EXT_PATH
+    includes = [*cpp_extension.include_paths(device_type="cuda"), sysconfig.get_paths()["include"], str(INCLUDE_DIR)]
+    lib_dirs = [str(PKG_DIR), *cpp_extension.library_paths(device_type="cuda")]
+    torch_lib = str(Path(torch.__file__).resolve().parent / "lib")
+    tmp = EXT_PATH.with_suffix(".so.tmp")
+    cmd = [
+        os.environ.get("CXX", "g++"),
+        "-O2",
+        "-std=c++17",
+        "-fPIC",
+        "-shared",
+        f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+        f"-DTORCH_EXTENSION_NAME={EXT_NAME}",
+        "-DTORCH_API_INCLUDE_EXTENSION_H",
+        *(f"-I{d}" for d in includes),
+        str(EXT_SOURCE),
+        "-o",
+        str(tmp),
+        *(f"-L{d}" for d in lib_dirs),
+        "-lnie_b200",
+        "-lc10",
+        "-lc10_cuda",
+        "-ltorch",
+        "-ltorch_cpu",
+        "-ltorch_cuda",
+        "-ltorch_python",
+        "-Wl,-rpath,$ORIGIN",
+        f"-Wl,-rpath,{torch_lib}",
+    ]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"g++ failed for {EXT_SOURCE.name}:\n{proc.stdout}\n{proc.stderr}")
+    os.replace(tmp, EXT_PATH)
+    if verbose:
+        print(f"built {EXT_PATH}")
+    return EXT_PATH
+
+
 if __name__ == "__main__":
     import sys
 
     build(force="--force" in sys.argv, verbose=True)
+    build_ext(force="--force" in sys.argv, verbose=True)

@@ -28,6 +28,7 @@ import torch
 from torch import nn
 
 from .. import ops
+from ..layers.attention import fused_weight
 from ..layers.decoder import Llama3Decoder
 from ..layers.rms_norm import RmsNorm
 from ..layers.rope import Rope, RopeScale
@@ -191,6 +192,9 @@ class Llama3_2(nn.Module):
 
     # Replay decode-only steps from captured CUDA graphs (one per batch size).
     cuda_graphs: bool = True
+    # Run the decoder layers of a ragged step through the C++ layer loop when
+    # it is built (the Python loop issues the same kernels, with more host time).
+    native_layer_loop: bool = True
 
     def __init__(self, config: LlamaConfig) -> None:
         super().__init__()
@@ -236,6 +240,11 @@ class Llama3_2(nn.Module):
         x = ops.embed_rows(input_ids, table) if ops.embed_eligible(table) else self.embed(input_ids)
         positions = meta.positions if rope_positions is None else rope_positions
         sin, cos = self.rope.sin_cos(positions, x.dtype)
+        ext = ops.layer_loop_ext() if (self.native_layer_loop and x.is_cuda) else None
+        layer_args = self._layer_loop_args(x.dtype) if ext is not None else None
+        if layer_args is not None:
+            normed = self._run_layers_native(ext, layer_args, x, meta, cache, sin, cos, logit_rows)
+            return self.lm_head(normed)
         first = self.decoders[0].pre_norm
         residual = x
         _, normed = ops.add_rmsnorm(x, None, first.weight, first.eps)
@@ -251,6 +260,60 @@ class Llama3_2(nn.Module):
                     h = h.index_select(0, logit_rows)
                 _, normed = ops.add_rmsnorm(mlp_out, h, self.final_rms.weight, self.final_rms.eps, want_sum=False)
         return self.lm_head(normed)
+
+    def _layer_loop_args(self, dtype: torch.dtype) -> tuple[list[torch.Tensor], list[float]] | None:
+        """Per-layer weights for the C++ layer loop, or None where the Python loop must run.
+
+        Rebuilt every step from the module dictionaries, with the same checks
+        as the Python loop: fused q/k/v and gate/up buffers still back the
+        projection weights, no forward hooks on o_proj / down_proj (or global
+        ones) and no biases, so both loops compute the same thing.
+        """
+        hooks = nn.modules.module
+        if hooks._global_forward_hooks or hooks._global_forward_pre_hooks:
+            return None
+        weights: list[torch.Tensor] = []
+        eps: list[float] = []
+        for decoder in self.decoders:
+            mods = decoder.__dict__["_modules"]
+            attn, ffn = mods["attn"], mods["ffn"]
+            qkv = fused_weight(attn, ("q_proj", "k_proj", "v_proj"), "_qkv")
+            gate_up = fused_weight(ffn, ("gate_proj", "up_proj"), "_gate_up")
+            if qkv is None or gate_up is None or qkv.dtype != dtype:
+                return None
+            o_proj, down = attn.__dict__["_modules"]["o_proj"], ffn.__dict__["_modules"]["down_proj"]
+            if o_proj._forward_hooks or o_proj._forward_pre_hooks or down._forward_hooks or down._forward_pre_hooks:
+                return None
+            o_params, down_params = o_proj._parameters, down._parameters
+            if o_params["bias"] is not None or down_params["bias"] is not None:
+                return None
+            pre, post = mods["pre_norm"], mods["post_norm"]
+            weights += (pre._parameters["weight"], qkv, o_params["weight"], post._parameters["weight"], gate_up,
+                        down_params["weight"])
+            eps += (pre.eps, post.eps)
+        return weights, eps
+
+    def _run_layers_native(self, ext, layer_args, x, meta, cache, sin, cos, logit_rows) -> torch.Tensor:
+        """All decoder layers and the final norm through the C++ layer loop."""
+        weights, eps = layer_args
+        attn = self.decoders[0].attn
+        hq, h, d = attn.q_head_num, attn.kv_head_num, attn.head_dim
+        keys = cache.keys
+        device = x.device
+        dec_ws = ops.decode_workspace(device, max(meta.num_decode, 1), hq, d)
+        var_ws = None
+        if meta.num_prefill:
+            need = int(ops.lib.nie_varlen_workspace_size(meta.num_prefill, meta.max_query_len, meta.max_seq_len, hq))
+            var_ws = ops.varlen_workspace(device, need) if need else None
+        normed, launches = ext.run_layers(
+            x, weights, eps, self.final_rms.weight, self.final_rms.eps,
+            meta.slot_mapping, meta.block_tables, meta.seq_lens, meta.query_start_loc, meta.table_rows,
+            meta.decode_list, meta.prefill_list, meta.num_decode, meta.num_prefill, meta.max_query_len,
+            meta.max_seq_len, logit_rows, keys, cache.values, sin, cos, hq, h, d, self.decoders[0].ffn.inner_size,
+            dec_ws, ops.decode_launch_count(keys.dtype, keys.shape[2], h, d, hq), var_ws, ops.error_flag(device),
+        )
+        ops._count(launches)
+        return normed
 
     def _ensure_fused(self) -> int:
         """Keep q/k/v and gate/up weights in single buffers; returns their generation.

@@ -9,7 +9,10 @@ is no CPU implementation.  Shapes follow the reference's cache layout
 from __future__ import annotations
 
 import ctypes
+import importlib.machinery
+import importlib.util
 from dataclasses import dataclass
+from pathlib import Path
 
 import torch
 
@@ -496,8 +499,7 @@ def paged_decode(
         _stream(device),
     )
     check(status, "nie_paged_decode")
-    fast = query.dtype == torch.bfloat16 and d == 64 and bs == 16 and hq // h <= 16 and h <= 16
-    _count(2 if fast else 1)
+    _count(decode_launch_count(query.dtype, bs, h, d, hq))
     return out
 
 
@@ -767,3 +769,32 @@ def argmax_rows(logits: torch.Tensor) -> torch.Tensor:
     check(status, "nie_argmax_rows")
     _count()
     return out
+
+
+# ------------------------------------------------------ layer-loop extension
+_LAYER_LOOP_PATH = Path(__file__).resolve().parent / "_nie_torch_ext.so"
+_layer_loop: object = None
+
+
+def layer_loop_ext():
+    """The torch C++ extension whose ``run_layers`` drives every decoder layer of
+    a ragged step in one call (same kernels and cuBLAS GEMMs as the Python
+    loop), or None when it has not been built (``_build.build_ext``).  A file
+    that exists but does not load (built against another torch) raises."""
+    global _layer_loop
+    if _layer_loop is None:
+        if not _LAYER_LOOP_PATH.exists():
+            _layer_loop = False
+        else:
+            loader = importlib.machinery.ExtensionFileLoader("_nie_torch_ext", str(_LAYER_LOOP_PATH))
+            spec = importlib.util.spec_from_loader("_nie_torch_ext", loader)
+            module = importlib.util.module_from_spec(spec)
+            loader.exec_module(module)
+            _layer_loop = module
+    return _layer_loop or None
+
+
+def decode_launch_count(dtype: torch.dtype, block_size: int, kv_heads: int, head_dim: int, q_heads: int) -> int:
+    """Kernels one :func:`paged_decode` call launches (split-K kernel + combine, or the generic one)."""
+    fast = dtype == torch.bfloat16 and head_dim == 64 and block_size == 16 and q_heads // kv_heads <= 16 and kv_heads <= 16
+    return 2 if fast else 1

@@ -154,7 +154,8 @@ def _generate(model, cfg, prompts, cuda, *, graphs, chunk):
     from nano_infer_engine_b200.paged_cache import PagedKVCache
 
     model.cuda_graphs = graphs
-    cache = PagedKVCache(256, 16, cfg.num_layers, cfg.kv_head_num, cfg.head_dim, torch.bfloat16, cuda)
+    dtype = model.embed.weight.dtype
+    cache = PagedKVCache(256, 16, cfg.num_layers, cfg.kv_head_num, cfg.head_dim, dtype, cuda)
     config = GenerationConfig(max_new_tokens=12, prefill_chunk_size=chunk, max_prefill_tokens_per_step=64 if chunk else None)
     sched = ContinuousBatchingScheduler(model, config, cache, 4)
     reqs = [sched.add_request(f"r{i}", p) for i, p in enumerate(prompts)]
@@ -163,6 +164,9 @@ def _generate(model, cfg, prompts, cuda, *, graphs, chunk):
         while sched.has_work:
             sched.step()
             logits.extend(r.last_logits.float().cpu() for r in sched.active_requests if r.last_logits is not None)
+    # the scheduler marks a request FAILED (instead of raising) when its step throws
+    assert [(r.status.value, r.error) for r in reqs] == [("completed", None)] * len(reqs)
+    assert all(r.generated_tokens == config.max_new_tokens for r in reqs)
     return [r.sequence[0].tolist() for r in reqs], logits, cache
 
 
@@ -182,4 +186,31 @@ def test_cuda_graph_decode_matches_eager(cuda, chunk):
     for a, b in zip(graph_logits, eager_logits):
         torch.testing.assert_close(a, b, atol=1e-2, rtol=0)
     assert getattr(cache, "_decode_graphs", None), "no decode step was captured"
+    assert cache.allocator.allocated_block_count == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_native_layer_loop_matches_python_loop(cuda, dtype):
+    """The C++ layer loop issues the Python loop's kernels and GEMMs: identical logits, bit for bit."""
+    from nano_infer_engine_b200 import ops
+    from nano_infer_engine_b200.models.llama import LlamaConfig, build_random_llama
+
+    assert ops.layer_loop_ext() is not None, "the layer-loop extension was not built"
+    cfg = LlamaConfig(vocab_size=512, hidden_size=512, mlp_inner_size=1024, num_layers=3, q_head_num=8,
+                      kv_head_num=2, max_seq_len=4096)
+    model = build_random_llama(cfg, 11, 0.02, dtype, cuda)
+    model._ensure_fused()
+    assert model._layer_loop_args(dtype) is not None
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg.vocab_size, (1, n), generator=g).to(cuda) for n in (3, 45, 130, 16)]
+    results = []
+    for native in (False, True):
+        model.native_layer_loop = native
+        results.append(_generate(model, cfg, prompts, cuda, graphs=False, chunk=32))
+    ops.check_device_errors(cuda)
+    (py_tokens, py_logits, _), (cc_tokens, cc_logits, cache) = results
+    assert cc_tokens == py_tokens
+    assert len(cc_logits) == len(py_logits)
+    for a, b in zip(cc_logits, py_logits):
+        assert torch.equal(a, b)
     assert cache.allocator.allocated_block_count == 0
