@@ -330,6 +330,21 @@ int nie_argmax_rows(const void* logits, int64_t rows, int64_t cols,
                     int64_t row_stride, int32_t dtype, int64_t* out,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * nie_linear: y[m, n] = x[m, k] . w[n, k]^T for decode-size batches (the
+ * nn.Linear projections of a decode step: layers/attention.py:121-145 q/k/v
+ * and o, layers/mlp.py:18-22 gate/up and down).  bf16 in and out, fp32
+ * accumulation, one rounding of each output.  Takes m <= 16, n % 128 == 0,
+ * k % 64 == 0, x and w 16-byte aligned with row strides ldx (a multiple of 8
+ * elements) and k, y rows at ldy (even); anything else returns
+ * NIE_ERR_UNSUPPORTED so the caller can use a library GEMM.  The weights are
+ * streamed once over all SMs (K split across a thread-block cluster where n
+ * is small); no workspace.  Results are deterministic.
+ */
+int nie_linear(const void* x, int64_t ldx, const void* w, int64_t n, int64_t k,
+               int64_t m, void* y, int64_t ldy, int32_t dtype,
+               int32_t* err_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

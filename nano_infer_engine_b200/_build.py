@@ -25,6 +25,7 @@ SOURCES = (
     "nie_attn_decode.cu",
     "nie_attn_prefill.cu",
     "nie_fused.cu",
+    "nie_linear.cu",
 )
 
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")

@@ -85,6 +85,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "nie_embed_rows": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "nie_argmax_workspace_size": (c_size_t, []),
     "nie_argmax_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "nie_linear": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int32, c_void_p, c_void_p],
+    ),
     "nie_varlen_workspace_size": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "nie_varlen_attention": (
         c_int,

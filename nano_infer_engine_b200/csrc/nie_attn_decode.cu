@@ -34,7 +34,8 @@ namespace nie {
 constexpr int kDecBS = 16;
 constexpr int kDecHD = 64;
 constexpr int kTileBytes = kDecBS * kDecHD * 2;  // one (block, head) tile: 2 KiB
-constexpr int kDecStages = 4;
+constexpr int kDecStages = 4;       // pipeline depth per warp for kv_heads <= 8
+constexpr int kDecStagesWide = 3;   // kv_heads 9..16 (shared memory bound)
 constexpr int kDecCtasPerSm = 1;
 constexpr int kDecMaxReq = 8192;
 constexpr uint32_t kWaitProbes = 1u << 22;
@@ -113,10 +114,22 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(dsm + nw * NST * 2 * kTileBytes);
   int* cum = reinterpret_cast<int*>(bars + nw * NST);
   const int R = a.num_req;
+  int* reqs = cum + R + 1;   // request index of list entry i
+  int* trows = reqs + R;     // its block-table row
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+  }
 
+  // Per-request metadata into shared memory up front: one dependent global
+  // load (the request list) before the lengths and table rows, which load in
+  // parallel; the block walk below then reads only the block tables.
   for (int i = threadIdx.x; i < R; i += blockDim.x) {
     const int r = a.req_list ? a.req_list[i] : i;
     const int n = a.seq_lens[r];
+    const int trow = a.table_rows ? a.table_rows[r] : r;
+    reqs[i] = r;
+    trows[i] = trow;
     cum[i] = n > 0 ? (n + kDecBS - 1) / kDecBS : 0;
   }
   __syncthreads();
@@ -137,10 +150,6 @@ __global__ void __launch_bounds__(512, 1)
   const int gb1 = min(total, gb0 + W);
   if (gb0 >= gb1) return;
 
-  if (lane == 0) {
-    prefetch_tensormap(&kmap);
-    prefetch_tensormap(&vmap);
-  }
   uint8_t* my_tiles = tiles + warp * NST * 2 * kTileBytes;
   uint64_t* my_bars = bars + warp * NST;
   const uint64_t policy = l2_policy_evict_first();
@@ -162,8 +171,7 @@ __global__ void __launch_bounds__(512, 1)
     int blk = 0;
     if (g < gb1) {
       const int i = locate(g);
-      const int req = a.req_list ? a.req_list[i] : i;
-      const int trow = a.table_rows ? a.table_rows[req] : req;
+      const int trow = trows[i];
       const int64_t lb = g - cum[i];
       int64_t b = (lb < a.tstride) ? (int64_t)a.tables[(int64_t)trow * a.tstride + lb] : -1;
       if (b < 0 || b >= a.nb) {
@@ -200,7 +208,7 @@ __global__ void __launch_bounds__(512, 1)
   int64_t qrow = 0;
 
   auto begin_request = [&](int i) {
-    const int req = a.req_list ? a.req_list[i] : i;
+    const int req = reqs[i];
     n_tok = a.seq_lens[req];
     qrow = a.q_rows ? a.q_rows[req] : (int64_t)req;
     const __nv_bfloat16* qp = a.q + qrow * a.q_stride + (int64_t)warp * G * kDecHD;
@@ -389,9 +397,14 @@ __global__ void __launch_bounds__(512, 1)
 }
 
 // Merge the partials of requests whose blocks were split across CTAs.
-// grid = (requests, q_heads), one thread per head-dim element: every load of
-// a split is independent of the others (the chain is only the final sums).
+// grid = (requests, q_heads), one thread per head-dim element.  The loads are
+// batched so that the merge takes a few memory round trips whatever the number
+// of splits: the split maxima in one pass (one per thread, reduced across the
+// CTA), then the weighted sums in chunks of 8 splits whose loads are all in
+// flight together.  The sums run in split order, as an unbatched loop would.
 __global__ void __launch_bounds__(kDecHD) decode_combine_kernel(DecodeArgs a) {
+  constexpr int kChunk = 8;
+  __shared__ float red[kDecHD / 32];
   const int i = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int R = a.num_req;
   const int32_t* cum = a.cum_out;
@@ -406,15 +419,32 @@ __global__ void __launch_bounds__(kDecHD) decode_combine_kernel(DecodeArgs a) {
   const float* base = a.partials + (int64_t)(c0 + i) * stride;
   const int n = c1 - c0 + 1;
   float M = -INFINITY;
-#pragma unroll 4
-  for (int c = 0; c < n; ++c) M = fmaxf(M, base[c * stride + h]);
+  for (int c = d; c < n; c += kDecHD) M = fmaxf(M, base[c * stride + h]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if ((d & 31) == 0) red[d >> 5] = M;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kDecHD / 32; ++w) M = fmaxf(M, red[w]);
   float L = 0.f, O = 0.f;
-#pragma unroll 4
-  for (int c = 0; c < n; ++c) {
-    const float* ps = base + c * stride;
-    const float w = fast_exp2(ps[h] - M);
-    L += ps[a.hq + h] * w;
-    O += ps[2 * a.hq + h * kDecHD + d] * w;
+  for (int c = 0; c < n; c += kChunk) {
+    float mv[kChunk], lv[kChunk], ov[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      const float* ps = base + (int64_t)(c + j) * stride;
+      const bool ok = c + j < n;
+      mv[j] = ok ? ps[h] : -INFINITY;
+      lv[j] = ok ? ps[a.hq + h] : 0.f;
+      ov[j] = ok ? ps[2 * a.hq + h * kDecHD + d] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      if (c + j < n) {
+        const float w = fast_exp2(mv[j] - M);
+        L += lv[j] * w;
+        O += ov[j] * w;
+      }
+    }
   }
   a.out[qrow * a.out_stride + (int64_t)h * kDecHD + d] = __float2bfloat16_rn(O / L);
 }
@@ -425,9 +455,17 @@ static size_t ws_bytes(int grid, int R, int hq) {
   return ws_header_bytes(R) + (size_t)(grid + R) * hq * (kDecHD + 2) * sizeof(float);
 }
 
+static int decode_stages(int hkv) { return hkv <= 8 ? kDecStages : kDecStagesWide; }
+
 static size_t decode_smem_bytes(int hkv, int R) {
-  return 1024 + (size_t)hkv * kDecStages * 2 * kTileBytes + (size_t)hkv * kDecStages * 8 + (size_t)(R + 1) * 4;
+  const int nst = decode_stages(hkv);
+  // tiles, barriers, then cum[R + 1], reqs[R] and trows[R]
+  return 1024 + (size_t)hkv * nst * 2 * kTileBytes + (size_t)hkv * nst * 8 + (size_t)(3 * R + 1) * 4;
 }
+
+// Dynamic shared memory the decode CTA may use: the 227 KiB opt-in limit of
+// sm_100 less a margin for the kernel's static shared memory.
+constexpr size_t kMaxDynSmem = 232448 - 1024;
 
 }  // namespace nie
 
@@ -473,7 +511,8 @@ extern "C" int nie_paged_decode(const void* q, int64_t q_row_stride, void* out, 
                     workspace_bytes >= ws_bytes(grid, num_requests, q_heads) && aligned(q, 4) && aligned(out, 4) &&
                     (q_row_stride % 2) == 0 && (out_row_stride % 2) == 0 && aligned(key_cache, 16) &&
                     aligned(value_cache, 16) && aligned(workspace, 256) &&
-                    num_blocks * kDecBS < (int64_t(1) << 31);
+                    num_blocks * kDecBS < (int64_t(1) << 31) &&
+                    decode_smem_bytes(kv_heads, num_requests) <= kMaxDynSmem;
   if (!fast) {
     GenericArgs ga{};
     ga.q = q;
@@ -537,14 +576,11 @@ extern "C" int nie_paged_decode(const void* q, int64_t q_row_stride, void* out, 
   da.err = err_flag;
 
   const size_t smem = decode_smem_bytes(kv_heads, num_requests);
-  static thread_local size_t s_smem_set = 0;
-  if (smem > s_smem_set) {
-    cudaError_t e = cudaFuncSetAttribute(decode_tma_kernel<kDecStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return fail(NIE_ERR_CUDA, "decode smem %zu: %s", smem, cudaGetErrorString(e));
-    s_smem_set = smem;
-  }
-  decode_tma_kernel<kDecStages><<<grid, kv_heads * 32, smem, s>>>(kmap, vmap, da);
+  const bool wide = decode_stages(kv_heads) != kDecStages;
+  auto* kernel = wide ? decode_tma_kernel<kDecStagesWide> : decode_tma_kernel<kDecStages>;
+  rc = opt_in_smem(wide ? kSmemDecodeWide : kSmemDecode, (const void*)kernel, smem);
+  if (rc != NIE_OK) return rc;
+  kernel<<<grid, kv_heads * 32, smem, s>>>(kmap, vmap, da);
   rc = check_launch("decode_tma_kernel");
   if (rc != NIE_OK) return rc;
   decode_combine_kernel<<<dim3((unsigned)num_requests, (unsigned)q_heads), kDecHD, 0, s>>>(da);

@@ -736,12 +736,8 @@ int launch_prefill_tc(const void* q, void* out, int64_t row_stride, int64_t num_
   pa.scale_pow2 = is_pow2_float(scale) ? 1 : 0;
   pa.err = err_flag;
   const size_t smem = prefill_smem_bytes();
-  static thread_local bool s_attr = false;
-  if (!s_attr) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return fail(NIE_ERR_CUDA, "prefill smem %zu: %s", smem, cudaGetErrorString(e));
-    s_attr = true;
-  }
+  const int orc = opt_in_smem(kSmemPrefill, (const void*)prefill_tc_kernel, smem);
+  if (orc != NIE_OK) return orc;
   int grid;
   if (pa.stream) {
     const int sms = sm_count(stream_device(s));

@@ -20,6 +20,16 @@ int fail(int code, const char* fmt, ...);
 int check_launch(const char* what);
 int sm_count(int device);
 int stream_device(cudaStream_t stream);
+// Shared-memory opt-in slots, one per kernel instance that needs > 48 KiB.
+enum SmemSlot {
+  kSmemDecode = 0,
+  kSmemDecodeWide = 1,
+  kSmemPrefill = 2,
+  kSmemLinear = 3,
+  kSmemLinear64 = 4,
+  kSmemSlots = 6
+};
+int opt_in_smem(int slot, const void* kernel, size_t bytes);
 
 #define NIE_REQUIRE(cond, ...)                                \
   do {                                                        \

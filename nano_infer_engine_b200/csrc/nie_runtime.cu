@@ -49,6 +49,24 @@ int sm_count(int device) {
   return g_sm_count[device];
 }
 
+// Raise `kernel`'s dynamic shared memory limit on the current device to at
+// least `bytes`, per (device, slot): function attributes belong to the
+// device's context, so a thread that drives two GPUs must set them on each.
+static size_t g_smem_opt_in[64][kSmemSlots];
+
+int opt_in_smem(int slot, const void* kernel, size_t bytes) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || slot < 0 || slot >= kSmemSlots)
+    return fail(NIE_ERR_CUDA, "cannot resolve the current device for a shared-memory opt-in");
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_smem_opt_in[dev][slot] < bytes) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return fail(NIE_ERR_CUDA, "shared memory opt-in of %zu bytes: %s", bytes, cudaGetErrorString(e));
+    g_smem_opt_in[dev][slot] = bytes;
+  }
+  return NIE_OK;
+}
+
 // Device whose SMs a launch on `stream` uses.  A kernel launch requires the
 // stream to belong to the current device, so the current device is the
 // answer; querying the stream itself (cudaStreamGetDevice) would invalidate a

@@ -9,9 +9,9 @@
 // exceeds the GPU time of a 512-token mixed step.  This file issues the same
 // launches from C++: the fused kernels through the library's C ABI
 // (include/nie_b200.h) with the arguments the Python wrappers pass, and the
-// projections through at::linear, i.e. the same cuBLAS calls as
-// torch.nn.functional.linear, so the results are identical to the Python
-// loop's.
+// projections through nie_linear (batches of <= 16 rows) or at::linear, the
+// same choice and calls as ops.linear, so the results are identical to the
+// Python loop's.
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
@@ -50,6 +50,33 @@ std::pair<at::Tensor, at::Tensor> add_rmsnorm(const at::Tensor& x, const at::Ten
   return {residual ? (sum.defined() ? sum : at::Tensor()) : x, out};
 }
 
+// x @ w^T: decode-size bf16 batches of long-K matrices on nie_linear (the
+// choice the Python loop's ops.linear makes), everything else at::linear.
+struct Linear {
+  bool enabled = false;
+  int32_t* err = nullptr;
+  void* stream = nullptr;
+  int64_t launches = 0;
+
+  at::Tensor operator()(const at::Tensor& x, const at::Tensor& w) {
+    const int64_t m = x.size(0), n = w.size(0), k = w.size(1);
+    // long-K matrices only (K >= 2N), where the cluster K split beats cuBLAS
+    if (enabled && m >= 1 && m <= 16 && k >= 2 * n && x.scalar_type() == at::kBFloat16 &&
+        w.scalar_type() == at::kBFloat16 &&
+        x.stride(1) == 1 && w.is_contiguous() && x.size(1) == k) {
+      at::Tensor y = at::empty({m, n}, x.options());
+      const int st =
+          nie_linear(x.data_ptr(), x.stride(0), w.data_ptr(), n, k, m, y.data_ptr(), n, NIE_DTYPE_BF16, err, stream);
+      if (st == NIE_OK) {
+        ++launches;
+        return y;
+      }
+      TORCH_CHECK(st == NIE_ERR_UNSUPPORTED, "nie_linear failed (status ", st, "): ", nie_last_error());
+    }
+    return at::linear(x, w);
+  }
+};
+
 }  // namespace
 
 // Returns the final normed hidden rows (of `logit_rows` when given) and the
@@ -60,7 +87,8 @@ std::pair<at::Tensor, at::Tensor> add_rmsnorm(const at::Tensor& x, const at::Ten
 // slot_mapping and query_start_loc, int32 tables, lengths and request
 // lists); dec_ws / var_ws are the decode and varlen scratch buffers sized by
 // nie_paged_decode_workspace_size / nie_varlen_workspace_size for this step,
-// and decode_launches the number of kernels one decode call launches.
+// and decode_launches the number of kernels one decode call launches;
+// stream_linear sends projections of <= 16 rows to nie_linear (else cuBLAS).
 std::tuple<at::Tensor, int64_t> run_layers(
     const at::Tensor& x, const std::vector<at::Tensor>& weights, const std::vector<double>& eps,
     const at::Tensor& final_w, double final_eps, const at::Tensor& slot_mapping, const at::Tensor& block_tables,
@@ -69,7 +97,7 @@ std::tuple<at::Tensor, int64_t> run_layers(
     int64_t max_seq_len, const c10::optional<at::Tensor>& logit_rows, const at::Tensor& keys,
     const at::Tensor& values, const at::Tensor& sin, const at::Tensor& cos, int64_t q_heads, int64_t kv_heads,
     int64_t head_dim, int64_t inner, const at::Tensor& dec_ws, int64_t decode_launches,
-    const c10::optional<at::Tensor>& var_ws, const at::Tensor& err) {
+    const c10::optional<at::Tensor>& var_ws, bool stream_linear, const at::Tensor& err) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "x must be a contiguous CUDA [T, hidden] tensor");
   TORCH_CHECK(keys.dim() == 5 && keys.is_contiguous() && values.is_contiguous() && keys.sizes() == values.sizes() &&
                   keys.scalar_type() == x.scalar_type() && values.scalar_type() == x.scalar_type(),
@@ -95,6 +123,10 @@ std::tuple<at::Tensor, int64_t> run_layers(
   const float scale = (float)(1.0 / std::sqrt((double)head_dim));
   const size_t var_bytes = var_ws.has_value() ? (size_t)var_ws->numel() : 0;
   int64_t launches = 0;
+  Linear linear;
+  linear.enabled = stream_linear;
+  linear.err = err.data_ptr<int32_t>();
+  linear.stream = stream;
 
   at::Tensor residual = x;
   auto [unused, normed] = add_rmsnorm(x, nullptr, weights[0], eps[0], false, stream);
@@ -108,7 +140,7 @@ std::tuple<at::Tensor, int64_t> run_layers(
     const at::Tensor& gu_w = weights[6 * li + 4];
     const at::Tensor& down_w = weights[6 * li + 5];
     // q/k/v, RoPE on q and k, k/v into the cache slots
-    at::Tensor qkv = at::linear(normed, qkv_w);
+    at::Tensor qkv = linear(normed, qkv_w);
     at::Tensor q = qkv.narrow(1, 0, nq), k = qkv.narrow(1, nq, nkv), v = qkv.narrow(1, nq + nkv, nkv);
     at::Tensor q_rot = at::empty({T, q_heads, head_dim}, x.options());
     check(nie_rope_write_kv(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
@@ -141,18 +173,18 @@ std::tuple<at::Tensor, int64_t> run_layers(
             "nie_varlen_attention");
       launches += var_bytes ? 2 : 1;
     }
-    at::Tensor attn = at::linear(att.view({T, hidden}), o_w);
+    at::Tensor attn = linear(att.view({T, hidden}), o_w);
     // h = attn + residual, normed2 = post-norm(h)
     auto [h, normed2] = add_rmsnorm(attn, &residual, post_w, eps[2 * li + 1], true, stream);
     ++launches;
-    at::Tensor gate_up = at::linear(normed2, gu_w);
+    at::Tensor gate_up = linear(normed2, gu_w);
     at::Tensor gate = gate_up.narrow(1, 0, inner), up = gate_up.narrow(1, inner, inner);
     at::Tensor act = at::empty({T, inner}, x.options());
     check(nie_silu_mul(gate.data_ptr(), gate.stride(0), up.data_ptr(), up.stride(0), act.data_ptr(), T,
                        (int32_t)inner, dt, stream),
           "nie_silu_mul");
     ++launches;
-    at::Tensor mlp = at::linear(act, down_w);
+    at::Tensor mlp = linear(act, down_w);
     if (li + 1 < n_layers) {
       auto [sum, nxt] = add_rmsnorm(mlp, &h, weights[6 * (li + 1)], eps[2 * (li + 1)], true, stream);
       ++launches;
@@ -169,7 +201,7 @@ std::tuple<at::Tensor, int64_t> run_layers(
       out_final = fin;
     }
   }
-  return {out_final, launches};
+  return {out_final, launches + linear.launches};
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

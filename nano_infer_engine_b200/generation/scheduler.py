@@ -29,6 +29,22 @@ from .paged_prefill import _validate_paged_prefill_inputs, paged_prefill, paged_
 from .request import PagedRequest, RequestStatus
 
 
+class _PendingTokens:
+    """Sampled token ids on their way to the host: a pinned buffer filled by an
+    asynchronous copy, and the event that marks the copy's completion."""
+
+    def __init__(self, tokens: torch.Tensor) -> None:
+        flat = tokens.reshape(-1)
+        self.host = torch.empty(flat.shape, dtype=flat.dtype, pin_memory=True)
+        self.host.copy_(flat, non_blocking=True)
+        self.event = torch.cuda.Event()
+        self.event.record(torch.cuda.current_stream(flat.device))
+
+    def values(self) -> list[int]:
+        self.event.synchronize()
+        return self.host.tolist()
+
+
 class ContinuousBatchingScheduler:
     """Schedule dynamically submitted requests over one shared paged cache."""
 
@@ -289,7 +305,15 @@ class ContinuousBatchingScheduler:
         return tuple(cancelled)
 
     # --------------------------------------------------------------- steps
-    def _sample(self, requests: list[PagedRequest]) -> tuple[torch.Tensor, list[int]]:
+    def _sample(
+        self, requests: list[PagedRequest], *, defer: bool = False
+    ) -> tuple[torch.Tensor, list[int] | _PendingTokens]:
+        """Greedy next tokens on the device, and their values for the host.
+
+        ``defer`` (CUDA only) starts the copy to the host without waiting for
+        it: the caller can queue the next forward first and read the values
+        (``_PendingTokens.values``) while the GPU runs it.
+        """
         rows = []
         for request in requests:
             if request.last_logits is None:
@@ -303,20 +327,29 @@ class ContinuousBatchingScheduler:
             next_tokens = ops.argmax_rows(stacked).unsqueeze(-1)  # one launch, torch.argmax's answer
         else:
             next_tokens = stacked.argmax(dim=-1, keepdim=True)
+        if defer and next_tokens.is_cuda:
+            return next_tokens, _PendingTokens(next_tokens)
         return next_tokens, next_tokens.squeeze(-1).tolist()
 
     def _retire(
         self,
         requests: list[PagedRequest],
-        token_ids: list[int],
+        token_ids: list[int] | None,
         completed_now: list[PagedRequest],
     ) -> list[int]:
-        """Append sampled tokens; retire on EOS / token limit; return survivor indices."""
+        """Append sampled tokens; retire on EOS / token limit; return survivor indices.
+
+        ``token_ids`` None (no EOS configured, so only the token count decides)
+        leaves the appends to the caller, once the values have reached the host.
+        """
         eos = self.config.eos_token_id
+        if token_ids is None and eos is not None:
+            raise ValueError("token values are needed to check for the EOS token")
         survivors: list[int] = []
         for index, request in enumerate(requests):
             request.generated_tokens += 1
-            request.append_token(token_ids[index])
+            if token_ids is not None:
+                request.append_token(token_ids[index])
         for index, request in enumerate(requests):
             stopped = eos is not None and token_ids[index] == eos
             at_limit = request.generated_tokens >= self.config.max_new_tokens
@@ -346,8 +379,11 @@ class ContinuousBatchingScheduler:
             raise RuntimeError("pending requests cannot be admitted")
         completed_now: list[PagedRequest] = []
         decoding = list(self.active_requests)
-        next_tokens, token_ids = self._sample(decoding)
-        events = tuple(TokenEvent(r.sequence_id, token_ids[i]) for i, r in enumerate(decoding))
+        # Without an EOS token the schedule depends on token counts only, so the
+        # next forward is queued before the sampled values are read back: the
+        # host bookkeeping of this step then overlaps the GPU's next step.
+        next_tokens, sampled = self._sample(decoding, defer=self.config.eos_token_id is None)
+        token_ids = None if isinstance(sampled, _PendingTokens) else sampled
         keep = self._retire(decoding, token_ids, completed_now)
         survivors = [decoding[i] for i in keep]
         survivor_tokens = [next_tokens[i : i + 1] for i in keep]
@@ -371,6 +407,11 @@ class ContinuousBatchingScheduler:
                 self._finish_prefill_chunks(prefill_requests, prefill_chunks, logits[:n])
                 for request, row in zip(survivors, logits[n:]):
                     request.last_logits = row
+        if token_ids is None:
+            token_ids = sampled.values()
+            for request, token in zip(decoding, token_ids):
+                request.append_token(token)
+        events = tuple(TokenEvent(r.sequence_id, token_ids[i]) for i, r in enumerate(decoding))
         self.completed_requests.extend(completed_now)
         return SchedulerStepOutput(events, tuple(completed_now))
 

@@ -44,7 +44,7 @@ def apply_linear(module: nn.Linear, x: torch.Tensor) -> torch.Tensor:
             or nn.modules.module._global_forward_pre_hooks):
         return module(x)
     params = module._parameters
-    return torch.nn.functional.linear(x, params["weight"], params["bias"])
+    return ops.linear(x, params["weight"], params["bias"])
 
 
 def fuse_linears(module: nn.Module, names: tuple[str, ...], attr: str) -> bool:
@@ -107,7 +107,7 @@ class GroupedQueryAttention(nn.Module):
         """q/k/v projections, RoPE on q and k, k/v into the cache; returns q ``[T, Hq, D]``."""
         fused = fused_weight(self, ("q_proj", "k_proj", "v_proj"), "_qkv")
         if fused is not None:
-            qkv = torch.nn.functional.linear(x, fused)
+            qkv = ops.linear(x, fused)
             nq = self.q_head_num * self.head_dim
             nkv = self.kv_head_num * self.head_dim
             q, k, v = qkv[:, :nq], qkv[:, nq : nq + nkv], qkv[:, nq + nkv :]

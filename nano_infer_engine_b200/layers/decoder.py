@@ -45,7 +45,7 @@ class Llama3Decoder(nn.Module):
         h, normed2 = ops.add_rmsnorm(attn, residual, self.post_norm.weight, self.post_norm.eps)
         fused = fused_weight(self.ffn, ("gate_proj", "up_proj"), "_gate_up")
         if fused is not None:
-            gate_up = torch.nn.functional.linear(normed2, fused)
+            gate_up = ops.linear(normed2, fused)
             inner = self.ffn.inner_size
             gate, up = gate_up[:, :inner], gate_up[:, inner:]
         else:

@@ -310,7 +310,8 @@ class Llama3_2(nn.Module):
             meta.slot_mapping, meta.block_tables, meta.seq_lens, meta.query_start_loc, meta.table_rows,
             meta.decode_list, meta.prefill_list, meta.num_decode, meta.num_prefill, meta.max_query_len,
             meta.max_seq_len, logit_rows, keys, cache.values, sin, cos, hq, h, d, self.decoders[0].ffn.inner_size,
-            dec_ws, ops.decode_launch_count(keys.dtype, keys.shape[2], h, d, hq), var_ws, ops.error_flag(device),
+            dec_ws, ops.decode_launch_count(keys.dtype, keys.shape[2], h, d, hq), var_ws,
+            ops.STREAM_LINEAR, ops.error_flag(device),
         )
         ops._count(launches)
         return normed

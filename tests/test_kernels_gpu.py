@@ -161,9 +161,13 @@ def test_decode_matches_reference_golden(cuda, name):
     torch.testing.assert_close(out.cpu().float(), golden.float(), atol=tol, rtol=0)
 
 
-@pytest.mark.parametrize("seed,B,max_ctx", [(0, 64, 3000), (1, 7, 20000), (2, 130, 600), (3, 1, 29600)])
-def test_fast_decode_against_oracle(cuda, seed, B, max_ctx):
-    """bf16 / hd 64 / bs 16 split-K kernel, ragged lengths incl. 1 and block-aligned."""
+@pytest.mark.parametrize("seed,B,max_ctx,hkv", [(0, 64, 3000, 8), (1, 7, 20000, 8), (2, 130, 600, 8),
+                                                (3, 1, 29600, 8), (4, 20, 2500, 16)])
+def test_fast_decode_against_oracle(cuda, seed, B, max_ctx, hkv):
+    """bf16 / hd 64 / bs 16 split-K kernel, ragged lengths incl. 1 and block-aligned.
+
+    16 kv heads is the widest group layout the kernel takes (one warp per kv
+    head, a shallower pipeline so the CTA's tiles fit in shared memory)."""
     g = torch.Generator().manual_seed(seed)
     bs = 16
     lens = torch.randint(1, max_ctx + 1, (B,), generator=g).tolist()
@@ -173,8 +177,8 @@ def test_fast_decode_against_oracle(cuda, seed, B, max_ctx):
     total_blocks = sum((n + bs - 1) // bs for n in lens)
     nb = total_blocks + 37
     tables = _random_layout(nb, lens, bs, seed)
-    kc = torch.randn(1, nb, bs, 8, 64, generator=g).to(torch.bfloat16)
-    vc = torch.randn(1, nb, bs, 8, 64, generator=g).to(torch.bfloat16)
+    kc = torch.randn(1, nb, bs, hkv, 64, generator=g).to(torch.bfloat16)
+    vc = torch.randn(1, nb, bs, hkv, 64, generator=g).to(torch.bfloat16)
     q = torch.randn(B, 32, 64, generator=g).to(torch.bfloat16)
     dk, dv = kc.to(cuda), vc.to(cuda)
     # poison the unused tail rows: masked positions must not leak (NaN * 0)
@@ -443,3 +447,48 @@ def test_argmax_rows_matches_torch(cuda, dtype, rows, cols):
         assert torch.equal(got, x.argmax(dim=-1))
     view = x[:, : cols - 1] if cols > 1 else x  # row stride larger than the row
     assert torch.equal(ops().argmax_rows(view), view.argmax(dim=-1))
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 128, 64), (5, 3072, 2048), (16, 2048, 8192), (16, 16384, 2048),
+                                   (7, 640, 640), (16, 128, 8192)])
+def test_stream_linear_matches_fp32_reference(cuda, m, n, k):
+    """nie_linear (weight streaming, K split over a cluster, partials merged in shared memory) against torch fp32.
+
+    Tolerance: fp32 accumulation in a different order, then one bf16 rounding of
+    the output, so |err| <= 1 bf16 ulp of |y| plus fp32 noise: atol 1e-3 on
+    outputs of scale ~0.5, rtol 2^-7."""
+    g = torch.Generator().manual_seed(m * 7 + n + k)
+    x = (torch.randn(m, k, generator=g) * 0.5).to(torch.bfloat16).to(cuda)
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).to(torch.bfloat16).to(cuda)
+    before = ops().LAUNCHES
+    y = ops().linear_stream(x, w)
+    assert ops().LAUNCHES == before + 1
+    ops().check_device_errors(cuda)
+    ref = x.float() @ w.float().T
+    torch.testing.assert_close(y.float(), ref, atol=1e-3, rtol=2 ** -7)
+    # same bits on a second call (fixed merge order), also after a call of another shape
+    ops().linear_stream(x[:, :64].contiguous(), w[:128, :64].contiguous())
+    assert torch.equal(ops().linear_stream(x, w), y)
+    ops().check_device_errors(cuda)
+
+
+def test_stream_linear_strided_rows_and_routing(cuda):
+    """x rows with a stride (a column slice) use the kernel; ops.linear routes long-K
+    matrices to it and everything else (more rows, K < 2N, ragged N) to torch."""
+    g = torch.Generator().manual_seed(1)
+    big = torch.randn(9, 3072, generator=g).to(torch.bfloat16).to(cuda)
+    x = big[:, 1024:3072]
+    w = (torch.randn(256, 2048, generator=g) / 45).to(torch.bfloat16).to(cuda)
+    assert ops().linear_eligible(x, w)
+    torch.testing.assert_close(ops().linear(x, w).float(), x.float() @ w.float().T, atol=1e-3, rtol=2 ** -7)
+    before = ops().LAUNCHES
+    ops().linear(x, w)
+    assert ops().LAUNCHES == before + 1
+    x17 = torch.randn(17, 2048, generator=g).to(torch.bfloat16).to(cuda)
+    assert not ops().linear_eligible(x17, w)
+    assert torch.equal(ops().linear(x17, w), torch.nn.functional.linear(x17, w))
+    square = torch.randn(2048, 2048, generator=g).to(torch.bfloat16).to(cuda)
+    assert not ops().linear_eligible(x, square)
+    w100 = torch.randn(100, 2048, generator=g).to(torch.bfloat16).to(cuda)
+    assert not ops().linear_eligible(x, w100)
+    ops().check_device_errors(cuda)
