@@ -397,38 +397,32 @@ __global__ void __launch_bounds__(512, 1)
 }
 
 // Merge the partials of requests whose blocks were split across CTAs.
-// grid = (requests, q_heads), one thread per head-dim element.  The loads are
-// batched so that the merge takes a few memory round trips whatever the number
-// of splits: the split maxima in one pass (one per thread, reduced across the
-// CTA), then the weighted sums in chunks of 8 splits whose loads are all in
-// flight together.  The sums run in split order, as an unbatched loop would.
-__global__ void __launch_bounds__(kDecHD) decode_combine_kernel(DecodeArgs a) {
-  constexpr int kChunk = 8;
-  __shared__ float red[kDecHD / 32];
+// grid = (requests, q_heads), one thread per head-dim element.  A merge is
+// latency-bound (a handful of loads per thread, each an L2 round trip that may
+// cross the die boundary), so the loads are batched: the split bounds and the
+// output row in one round trip, then (m, l, O) of up to CHUNK splits at once;
+// the maximum is taken over the loaded values and the weighted sums run in
+// split order.  More splits take one more round trip per CHUNK.  CHUNK 16
+// needs twice the registers of CHUNK 8, so it is used only while the grid
+// still fits on the GPU in one wave.
+template <int CHUNK>
+__global__ void __launch_bounds__(kDecHD, CHUNK <= 8 ? 14 : 8) decode_combine_kernel(DecodeArgs a) {
+  constexpr int kChunk = CHUNK;
   const int i = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int R = a.num_req;
   const int32_t* cum = a.cum_out;
   const int W = cum[R + 1];
   const int lo = cum[i], hi = cum[i + 1];
+  const int req = a.req_list ? a.req_list[i] : i;
   if (hi <= lo || W <= 0) return;
   const int c0 = lo / W, c1 = (hi - 1) / W;
   if (c0 == c1) return;
-  const int req = a.req_list ? a.req_list[i] : i;
   const int64_t qrow = a.q_rows ? a.q_rows[req] : (int64_t)req;
   const int64_t stride = (int64_t)a.hq * (kDecHD + 2);
   const float* base = a.partials + (int64_t)(c0 + i) * stride;
   const int n = c1 - c0 + 1;
-  float M = -INFINITY;
-  for (int c = d; c < n; c += kDecHD) M = fmaxf(M, base[c * stride + h]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  if ((d & 31) == 0) red[d >> 5] = M;
-  __syncthreads();
-#pragma unroll
-  for (int w = 0; w < kDecHD / 32; ++w) M = fmaxf(M, red[w]);
-  float L = 0.f, O = 0.f;
-  for (int c = 0; c < n; c += kChunk) {
-    float mv[kChunk], lv[kChunk], ov[kChunk];
+  float mv[kChunk], lv[kChunk], ov[kChunk];
+  auto load = [&](int c) {
 #pragma unroll
     for (int j = 0; j < kChunk; ++j) {
       const float* ps = base + (int64_t)(c + j) * stride;
@@ -437,6 +431,14 @@ __global__ void __launch_bounds__(kDecHD) decode_combine_kernel(DecodeArgs a) {
       lv[j] = ok ? ps[a.hq + h] : 0.f;
       ov[j] = ok ? ps[2 * a.hq + h * kDecHD + d] : 0.f;
     }
+  };
+  load(0);
+  float M = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kChunk; ++j) M = fmaxf(M, mv[j]);
+  for (int c = kChunk; c < n; ++c) M = fmaxf(M, base[(int64_t)c * stride + h]);
+  float L = 0.f, O = 0.f;
+  for (int c = 0;;) {
 #pragma unroll
     for (int j = 0; j < kChunk; ++j) {
       if (c + j < n) {
@@ -445,6 +447,9 @@ __global__ void __launch_bounds__(kDecHD) decode_combine_kernel(DecodeArgs a) {
         O += ov[j] * w;
       }
     }
+    c += kChunk;
+    if (c >= n) break;
+    load(c);
   }
   a.out[qrow * a.out_stride + (int64_t)h * kDecHD + d] = __float2bfloat16_rn(O / L);
 }
@@ -583,7 +588,13 @@ extern "C" int nie_paged_decode(const void* q, int64_t q_row_stride, void* out, 
   kernel<<<grid, kv_heads * 32, smem, s>>>(kmap, vmap, da);
   rc = check_launch("decode_tma_kernel");
   if (rc != NIE_OK) return rc;
-  decode_combine_kernel<<<dim3((unsigned)num_requests, (unsigned)q_heads), kDecHD, 0, s>>>(da);
+  // 16-split batches while (requests x heads) CTAs of 64 threads at ~128
+  // registers fit in one wave (8 per SM), 8-split batches beyond
+  const dim3 cgrid((unsigned)num_requests, (unsigned)q_heads);
+  if ((int64_t)num_requests * q_heads <= (int64_t)sms * 8)
+    decode_combine_kernel<16><<<cgrid, kDecHD, 0, s>>>(da);
+  else
+    decode_combine_kernel<8><<<cgrid, kDecHD, 0, s>>>(da);
   return check_launch("decode_combine_kernel");
 }
 

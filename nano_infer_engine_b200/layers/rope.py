@@ -42,9 +42,26 @@ class Rope(nn.Module):
         i = torch.arange(0, self.dim, 2, dtype=torch.float32, device=device)
         return 1 / self.theta_base ** (i / self.dim)
 
+    def _freq_key(self) -> tuple:
+        return (self.dim, self.theta_base)
+
+    def cached_inv_freq(self, device: torch.device) -> torch.Tensor:
+        """:meth:`inv_freq`, computed once per device and parameter set (it is
+        the same ~10 torch ops every step otherwise).  Nothing is cached while
+        a CUDA graph is being captured, so the cache never holds graph-pool
+        memory."""
+        cache = self.__dict__.setdefault("_inv_freq_cache", {})
+        key = (device, self._freq_key())
+        freq = cache.get(key)
+        if freq is None:
+            freq = self.inv_freq(device)
+            if not (device.type == "cuda" and torch.cuda.is_current_stream_capturing()):
+                cache[key] = freq
+        return freq
+
     def sin_cos(self, positions: torch.Tensor, dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
         """sin/cos ``[..., T, D/2]`` for integer ``positions [..., T]`` cast to ``dtype``."""
-        angles = positions.to(dtype=torch.float32)[..., None] * self.inv_freq(positions.device)
+        angles = positions.to(dtype=torch.float32)[..., None] * self.cached_inv_freq(positions.device)
         return torch.sin(angles).to(dtype), torch.cos(angles).to(dtype)
 
     def forward(self, x: torch.Tensor, position_offset: int = 0, position_ids: torch.Tensor | None = None):
@@ -78,6 +95,10 @@ class RopeScale(Rope):
         self.low_freq_factor = low_freq_factor
         self.high_freq_factor = high_freq_factor
         self.original_max_position_embeddings = original_max_position_embeddings
+
+    def _freq_key(self) -> tuple:
+        return (self.dim, self.theta_base, self.scaling_factor, self.low_freq_factor, self.high_freq_factor,
+                self.original_max_position_embeddings)
 
     def inv_freq(self, device: torch.device) -> torch.Tensor:
         base = super().inv_freq(device)
