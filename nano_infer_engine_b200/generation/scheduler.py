@@ -429,8 +429,10 @@ class ContinuousBatchingScheduler:
             self.completed_requests.extend(completed_now)
             return SchedulerStepOutput((), tuple(completed_now))
         decoding = list(self.active_requests)
-        next_tokens, token_ids = self._sample(decoding)
-        events = tuple(TokenEvent(sequence_id=r.sequence_id, token_id=token_ids[i]) for i, r in enumerate(decoding))
+        # as in _step_unified_ragged: without an EOS token the next forward is
+        # queued before the sampled values are read back
+        next_tokens, sampled = self._sample(decoding, defer=self.config.eos_token_id is None)
+        token_ids = None if isinstance(sampled, _PendingTokens) else sampled
         keep = self._retire(decoding, token_ids, completed_now)
         survivors = [decoding[i] for i in keep]
         self.active_requests = survivors
@@ -446,6 +448,11 @@ class ContinuousBatchingScheduler:
             except Exception as error:
                 self._fail(survivors, error, completed_now)
                 self.active_requests = []
+        if token_ids is None:
+            token_ids = sampled.values()
+            for request, token in zip(decoding, token_ids):
+                request.append_token(token)
+        events = tuple(TokenEvent(sequence_id=r.sequence_id, token_id=token_ids[i]) for i, r in enumerate(decoding))
         completed_now.extend(self._admit_pending_requests())
         self.completed_requests.extend(completed_now)
         return SchedulerStepOutput(events, tuple(completed_now))

@@ -216,14 +216,15 @@ def test_native_layer_loop_matches_python_loop(cuda, dtype):
     assert cache.allocator.allocated_block_count == 0
 
 
-def test_eos_schedule_matches_eos_free_run_until_each_stop(cuda):
+@pytest.mark.parametrize("chunk", [32, None])
+def test_eos_schedule_matches_eos_free_run_until_each_stop(cuda, chunk):
     """With an EOS token the scheduler reads each step's tokens before queuing the next
     forward (synchronous path); without one it queues first (deferred path).  Both must
     produce the same tokens up to each request's first EOS, where it stops."""
     model, cfg = _llama_shaped_model(cuda, seed=13)
     g = torch.Generator().manual_seed(4)
     prompts = [torch.randint(0, cfg.vocab_size, (1, n), generator=g).to(cuda) for n in (6, 50, 21)]
-    free_tokens, _, _ = _generate(model, cfg, prompts, cuda, graphs=True, chunk=32)
+    free_tokens, _, _ = _generate(model, cfg, prompts, cuda, graphs=True, chunk=chunk)
     first = free_tokens[0][prompts[0].shape[1]:]
     eos = first[2]  # request 0 stops after three tokens
 
@@ -232,8 +233,8 @@ def test_eos_schedule_matches_eos_free_run_until_each_stop(cuda):
     from nano_infer_engine_b200.paged_cache import PagedKVCache
 
     cache = PagedKVCache(256, 16, cfg.num_layers, cfg.kv_head_num, cfg.head_dim, torch.bfloat16, cuda)
-    config = GenerationConfig(max_new_tokens=12, eos_token_id=eos, prefill_chunk_size=32,
-                              max_prefill_tokens_per_step=64)
+    config = GenerationConfig(max_new_tokens=12, eos_token_id=eos, prefill_chunk_size=chunk,
+                              max_prefill_tokens_per_step=64 if chunk else None)
     sched = ContinuousBatchingScheduler(model, config, cache, 4)
     reqs = [sched.add_request(f"r{i}", p) for i, p in enumerate(prompts)]
     with torch.inference_mode():
