@@ -59,7 +59,7 @@ def parse_args():
     p.add_argument("--decode-iters", type=int, default=20)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--only", choices=("all", "engine", "decode", "mixed", "pd-open"), default="all",
+    p.add_argument("--only", choices=("all", "engine", "decode", "mixed", "pd-open", "linear"), default="all",
                    help="engine: headline run only; decode: config-3 decode micro-bench only; "
                         "mixed: config-4 mixed step only (profiling); pd-open: config 5 open loop "
                         "(Poisson arrivals, TTFT/TPOT, transfer GB/s; even N >= 2)")
@@ -572,6 +572,56 @@ def mixed_config4(device, iters):
     return res
 
 
+def linear_decode_shapes(device, m=16, copies=16, reps=4):
+    """nie_linear against torch's cuBLAS GEMM on the decode projections of config 2.
+
+    Each shape runs over `copies` distinct weight matrices (more bytes than
+    L2 holds except for the smallest), replayed from a CUDA graph; the
+    time per call is the graph time / calls.  Algorithmic bytes per call =
+    the weight matrix (x and y are < 0.1 % of it).
+    """
+    from nano_infer_engine_b200 import ops
+
+    peak, _ = measured_peaks()
+    gen = torch.Generator(device=device).manual_seed(SEED)
+    rows = []
+    for name, n, k in (("qkv", 3072, 2048), ("o_proj", 2048, 2048), ("gate_up", 16384, 2048),
+                       ("down_proj", 2048, 8192)):
+        ws = [torch.randn(n, k, device=device, dtype=torch.bfloat16, generator=gen) * 0.02 for _ in range(copies)]
+        x = torch.randn(m, k, device=device, dtype=torch.bfloat16, generator=gen)
+        row = {"shape": name, "m": m, "n": n, "k": k, "weight_bytes": n * k * 2}
+        for impl, fn in (("cublas", torch.nn.functional.linear), ("nie_linear", ops.linear_stream)):
+            stream = torch.cuda.Stream(device)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                for w in ws:
+                    fn(x, w)
+                torch.cuda.synchronize(device)
+                with torch.cuda.graph(graph, stream=stream):
+                    for _ in range(reps):
+                        for w in ws:
+                            fn(x, w)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize(device)
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record()
+            for _ in range(5):
+                graph.replay()
+            t1.record()
+            torch.cuda.synchronize(device)
+            us = t0.elapsed_time(t1) * 1e3 / (5 * reps * copies)
+            row[impl] = {"us": us, "GB/s": n * k * 2 / us / 1e3, "frac": n * k * 2 / us / 1e3 / peak}
+            del graph
+        ref = torch.nn.functional.linear(x, ws[0]).float()
+        row["max_abs_diff_vs_cublas"] = (ops.linear_stream(x, ws[0]).float() - ref).abs().max().item()
+        rows.append(row)
+        del ws
+        torch.cuda.empty_cache()
+    ops.check_device_errors(device)
+    return rows
+
+
 def measured_peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -747,6 +797,10 @@ def main():
         return 0
     if args.only == "mixed":
         print(json.dumps(mixed_config4(device, args.decode_iters)))
+        return 0
+    if args.only == "linear":
+        for row in linear_decode_shapes(device):
+            print(json.dumps(row))
         return 0
     model = build_engine(device)
     host_prompts = [p.pin_memory() for p in workload(args.requests)]
