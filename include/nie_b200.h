@@ -189,6 +189,30 @@ int nie_paged_decode(const void* q, int64_t q_row_stride, void* out,
                      size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 /*
+ * nie_paged_decode_overlapped: nie_paged_decode whose split-K kernel may start
+ * (block-table walk, barrier setup) while the kernel issued just before it on
+ * `stream` is still running; it waits for that kernel before reading q or the
+ * caches.  Precondition: the block tables, table rows, seq_lens, q_rows and
+ * the request list must NOT be written by that immediately preceding kernel
+ * (the engine writes them in its packing kernel, many kernels earlier; q and
+ * the new cache rows come from the RoPE + KV write right before).  Same
+ * arguments, results and errors as nie_paged_decode.
+ */
+int nie_paged_decode_overlapped(const void* q, int64_t q_row_stride, void* out,
+                                int64_t out_row_stride, const void* key_cache,
+                                const void* value_cache, int32_t dtype,
+                                int32_t layer, int64_t num_layers,
+                                int64_t num_blocks, int32_t block_size,
+                                int32_t kv_heads, int32_t head_dim,
+                                int32_t q_heads, const int32_t* block_tables,
+                                int64_t table_stride, const int32_t* table_rows,
+                                const int32_t* seq_lens, const int64_t* q_rows,
+                                const int32_t* req_list, int32_t num_requests,
+                                float scale, void* workspace,
+                                size_t workspace_bytes, int32_t* err_flag,
+                                void* stream);
+
+/*
  * Allocation-free paged decode.  This entry point has no counterpart in the
  * reference engine; it exists for callers that cannot allocate device memory:
  * code that binds this C ABI from a host language with no device allocator of

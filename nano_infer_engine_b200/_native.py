@@ -64,6 +64,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         + [c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p]
         + [c_void_p, c_void_p, c_int32, c_float, c_void_p, c_size_t, c_void_p, c_void_p],
     ),
+    "nie_paged_decode_overlapped": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int32, c_int64]
+        + [c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p]
+        + [c_void_p, c_void_p, c_int32, c_float, c_void_p, c_size_t, c_void_p, c_void_p],
+    ),
     "nie_paged_decode_noalloc_capacity": (c_size_t, []),
     "nie_paged_decode_noalloc": (
         c_int,

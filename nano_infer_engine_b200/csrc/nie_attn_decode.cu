@@ -194,6 +194,10 @@ __global__ void __launch_bounds__(512, 1)
     }
   };
   refill(gb0);
+  // Everything above reads step metadata written before the previous kernel
+  // (RoPE + KV write) was launched; q and the newest cache rows come from that
+  // kernel, so wait for it before the first load of either.
+  pdl_wait();
   int iss = gb0;
   for (int st = 0; st < NST && iss < gb1; ++st, ++iss) issue(iss, st);
 
@@ -490,13 +494,15 @@ extern "C" size_t nie_paged_decode_workspace_size(int device, int32_t R, int32_t
 
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-extern "C" int nie_paged_decode(const void* q, int64_t q_row_stride, void* out, int64_t out_row_stride,
-                                const void* key_cache, const void* value_cache, int32_t dtype, int32_t layer,
-                                int64_t num_layers, int64_t num_blocks, int32_t block_size, int32_t kv_heads,
-                                int32_t head_dim, int32_t q_heads, const int32_t* block_tables, int64_t table_stride,
-                                const int32_t* table_rows, const int32_t* seq_lens, const int64_t* q_rows,
-                                const int32_t* req_list, int32_t num_requests, float scale, void* workspace,
-                                size_t workspace_bytes, int32_t* err_flag, void* stream) {
+// Shared body of nie_paged_decode and nie_paged_decode_overlapped; `overlap`
+// lets the split-K kernel start while the kernel before it is still running.
+static int paged_decode_impl(const void* q, int64_t q_row_stride, void* out, int64_t out_row_stride,
+                             const void* key_cache, const void* value_cache, int32_t dtype, int32_t layer,
+                             int64_t num_layers, int64_t num_blocks, int32_t block_size, int32_t kv_heads,
+                             int32_t head_dim, int32_t q_heads, const int32_t* block_tables, int64_t table_stride,
+                             const int32_t* table_rows, const int32_t* seq_lens, const int64_t* q_rows,
+                             const int32_t* req_list, int32_t num_requests, float scale, void* workspace,
+                             size_t workspace_bytes, int32_t* err_flag, void* stream, bool overlap) {
   NIE_REQUIRE(dtype_size(dtype) > 0, "unknown dtype %d", dtype);
   NIE_REQUIRE(q && out && key_cache && value_cache && block_tables && seq_lens, "null pointer argument");
   NIE_REQUIRE(layer >= 0 && layer < num_layers, "layer %d out of range", layer);
@@ -585,9 +591,16 @@ extern "C" int nie_paged_decode(const void* q, int64_t q_row_stride, void* out, 
   auto* kernel = wide ? decode_tma_kernel<kDecStagesWide> : decode_tma_kernel<kDecStages>;
   rc = opt_in_smem(wide ? kSmemDecodeWide : kSmemDecode, (const void*)kernel, smem);
   if (rc != NIE_OK) return rc;
-  kernel<<<grid, kv_heads * 32, smem, s>>>(kmap, vmap, da);
-  rc = check_launch("decode_tma_kernel");
-  if (rc != NIE_OK) return rc;
+  if (overlap) {
+    // dependent launch: the prologue overlaps the kernel before it (the RoPE +
+    // KV write), whose outputs are read only after pdl_wait()
+    const cudaError_t le = launch_after_trigger(kernel, dim3(grid), dim3(kv_heads * 32), smem, s, kmap, vmap, da);
+    if (le != cudaSuccess) return fail(NIE_ERR_CUDA, "decode_tma_kernel launch: %s", cudaGetErrorString(le));
+  } else {
+    kernel<<<grid, kv_heads * 32, smem, s>>>(kmap, vmap, da);
+    rc = check_launch("decode_tma_kernel");
+    if (rc != NIE_OK) return rc;
+  }
   // 16-split batches while (requests x heads) CTAs of 64 threads at ~128
   // registers fit in one wave (8 per SM), 8-split batches beyond
   const dim3 cgrid((unsigned)num_requests, (unsigned)q_heads);
@@ -596,6 +609,33 @@ extern "C" int nie_paged_decode(const void* q, int64_t q_row_stride, void* out, 
   else
     decode_combine_kernel<8><<<cgrid, kDecHD, 0, s>>>(da);
   return check_launch("decode_combine_kernel");
+}
+
+extern "C" int nie_paged_decode(const void* q, int64_t q_row_stride, void* out, int64_t out_row_stride,
+                                const void* key_cache, const void* value_cache, int32_t dtype, int32_t layer,
+                                int64_t num_layers, int64_t num_blocks, int32_t block_size, int32_t kv_heads,
+                                int32_t head_dim, int32_t q_heads, const int32_t* block_tables, int64_t table_stride,
+                                const int32_t* table_rows, const int32_t* seq_lens, const int64_t* q_rows,
+                                const int32_t* req_list, int32_t num_requests, float scale, void* workspace,
+                                size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  return paged_decode_impl(q, q_row_stride, out, out_row_stride, key_cache, value_cache, dtype, layer, num_layers,
+                           num_blocks, block_size, kv_heads, head_dim, q_heads, block_tables, table_stride,
+                           table_rows, seq_lens, q_rows, req_list, num_requests, scale, workspace, workspace_bytes,
+                           err_flag, stream, false);
+}
+
+extern "C" int nie_paged_decode_overlapped(const void* q, int64_t q_row_stride, void* out, int64_t out_row_stride,
+                                           const void* key_cache, const void* value_cache, int32_t dtype,
+                                           int32_t layer, int64_t num_layers, int64_t num_blocks, int32_t block_size,
+                                           int32_t kv_heads, int32_t head_dim, int32_t q_heads,
+                                           const int32_t* block_tables, int64_t table_stride,
+                                           const int32_t* table_rows, const int32_t* seq_lens, const int64_t* q_rows,
+                                           const int32_t* req_list, int32_t num_requests, float scale,
+                                           void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  return paged_decode_impl(q, q_row_stride, out, out_row_stride, key_cache, value_cache, dtype, layer, num_layers,
+                           num_blocks, block_size, kv_heads, head_dim, q_heads, block_tables, table_stride,
+                           table_rows, seq_lens, q_rows, req_list, num_requests, scale, workspace, workspace_bytes,
+                           err_flag, stream, true);
 }
 
 extern "C" int nie_varlen_attention(const void* q, void* out, int64_t row_stride, int64_t num_q_rows,

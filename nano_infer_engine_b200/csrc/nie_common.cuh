@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/nie_b200.h"
 
 namespace nie {
@@ -35,6 +37,32 @@ int opt_in_smem(int slot, const void* kernel, size_t bytes);
   do {                                                        \
     if (!(cond)) return ::nie::fail(NIE_ERR_INVALID, __VA_ARGS__); \
   } while (0)
+
+// --------------------------------------------- programmatic dependent launch
+// A kernel launched with launch_after_trigger() may start while the kernel
+// before it on the stream is still running, once every CTA of that kernel has
+// executed pdl_trigger() (or exited).  Before it reads anything that kernel
+// writes it must call pdl_wait(), which returns once the previous grid has
+// completed and its memory operations are visible.  Without the launch
+// attribute both instructions are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_after_trigger(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                 Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 inline int dtype_size(int dtype) {
   switch (dtype) {

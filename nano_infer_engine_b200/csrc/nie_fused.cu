@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(256) rope_write_kernel(
     T* __restrict__ q_out, T* __restrict__ kc, T* __restrict__ vc, int64_t layer_off, int64_t total_slots,
     const int64_t* __restrict__ slots, int32_t* __restrict__ err) {
   using N = Num<T>;
+  pdl_trigger();  // the attention kernel after this one may start its prologue
   const int64_t t = blockIdx.x;
   const int half = d / 2;
   const T* sr = sin + t * half;
@@ -235,6 +236,7 @@ __global__ void __launch_bounds__(256) rope_write_vec_kernel(
     T* __restrict__ q_out, T* __restrict__ kc, T* __restrict__ vc, int64_t layer_off, int64_t total_slots,
     const int64_t* __restrict__ slots, int32_t* __restrict__ err) {
   using N = Num<T>;
+  pdl_trigger();  // the attention kernel after this one may start its prologue
   constexpr int V = Vec16<T>::N;
   const int64_t t = blockIdx.x;
   const int half = d / 2;

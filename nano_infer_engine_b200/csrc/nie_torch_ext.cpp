@@ -152,13 +152,15 @@ std::tuple<at::Tensor, int64_t> run_layers(
     ++launches;
     at::Tensor att = at::empty_like(q_rot);
     if (num_decode) {
-      check(nie_paged_decode(q_rot.data_ptr(), q_rot.stride(0), att.data_ptr(), att.stride(0), keys.data_ptr(),
+      // follows the RoPE + KV write; the metadata comes from the packing kernel
+      check(nie_paged_decode_overlapped(q_rot.data_ptr(), q_rot.stride(0), att.data_ptr(), att.stride(0),
+                             keys.data_ptr(),
                              values.data_ptr(), dt, (int32_t)li, L, nb, (int32_t)bs, (int32_t)kv_heads,
                              (int32_t)head_dim, (int32_t)q_heads, block_tables.data_ptr<int32_t>(),
                              block_tables.stride(0), table_rows.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
                              qsl.data_ptr<int64_t>(), decode_list.data_ptr<int32_t>(), (int32_t)num_decode, scale,
                              dec_ws.data_ptr(), (size_t)dec_ws.numel(), err.data_ptr<int32_t>(), stream),
-            "nie_paged_decode");
+            "nie_paged_decode_overlapped");
       launches += decode_launches;
     }
     if (num_prefill) {

@@ -149,6 +149,7 @@ class GroupedQueryAttention(nn.Module):
                 q_rows=meta.query_start_loc,
                 req_list=meta.decode_list,
                 num_requests=meta.num_decode,
+                overlap=True,  # follows the RoPE + KV write; the metadata comes from the packing kernel
             )
         if meta.num_prefill:
             ops.varlen_attention(

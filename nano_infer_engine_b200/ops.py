@@ -453,8 +453,15 @@ def paged_decode(
     req_list: torch.Tensor | None = None,
     num_requests: int | None = None,
     scale: float | None = None,
+    overlap: bool = False,
 ) -> torch.Tensor:
-    """Single-token paged attention for ``query [rows, q_heads, head_dim]``."""
+    """Single-token paged attention for ``query [rows, q_heads, head_dim]``.
+
+    ``overlap`` launches through ``nie_paged_decode_overlapped``: the kernel may
+    start before the previous kernel on the stream ends, so that kernel must not
+    have written ``block_tables``, ``seq_lens``, ``table_rows``, ``q_rows`` or
+    ``req_list`` (it may have written the query and the caches).
+    """
     _require_cuda(query, key_cache, value_cache, block_tables, seq_lens, table_rows, q_rows, req_list)
     L, nb, bs, h, d = _cache_geometry(key_cache)
     if query.ndim != 3 or query.shape[2] != d or query.stride(2) != 1 or query.stride(1) != d:
@@ -471,7 +478,7 @@ def paged_decode(
         out = torch.empty_like(query)
     device = query.device
     ws = decode_workspace(device, max(R, 1), hq, d)
-    status = lib.nie_paged_decode(
+    status = (lib.nie_paged_decode_overlapped if overlap else lib.nie_paged_decode)(
         query.data_ptr(),
         query.stride(0),
         out.data_ptr(),

@@ -492,3 +492,37 @@ def test_stream_linear_strided_rows_and_routing(cuda):
     w100 = torch.randn(100, 2048, generator=g).to(torch.bfloat16).to(cuda)
     assert not ops().linear_eligible(x, w100)
     ops().check_device_errors(cuda)
+
+
+def test_overlapped_decode_sees_the_rope_kernel_writes(cuda):
+    """nie_paged_decode_overlapped right after the RoPE + KV write (its intended caller order):
+    the newest token's K/V and the rotated q come from that kernel, and the result must equal the
+    plain entry point's and the oracle's."""
+    from nano_infer_engine_b200.layers.rope import RopeScale
+
+    g = torch.Generator().manual_seed(77)
+    bs, hq, hkv, d = 16, 32, 8, 64
+    lens = [1, 37, 900, 16 * 9, 2048, 333]
+    B = len(lens)
+    nb = sum((n + bs - 1) // bs for n in lens) + 11
+    tables = _random_layout(nb, lens, bs, 77)
+    kc = torch.randn(1, nb, bs, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+    vc = torch.randn(1, nb, bs, hkv, d, generator=g).to(torch.bfloat16).to(cuda)
+    q = torch.randn(B, hq * d, generator=g).to(torch.bfloat16).to(cuda)
+    k = torch.randn(B, hkv * d, generator=g).to(torch.bfloat16).to(cuda)
+    v = torch.randn(B, hkv * d, generator=g).to(torch.bfloat16).to(cuda)
+    pos = torch.tensor([n - 1 for n in lens]).to(cuda)
+    slots = torch.tensor([t[(n - 1) // bs] * bs + (n - 1) % bs for t, n in zip(tables, lens)]).to(cuda)
+    tab = _tables_tensor(tables, cuda)
+    seq = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    sin, cos = RopeScale(d).sin_cos(pos, torch.bfloat16)
+    outs = []
+    for overlap in (True, False):
+        kk, vv = kc.clone(), vc.clone()
+        torch.cuda.synchronize()
+        qr = ops().rope_write_kv(q, k, v, sin, cos, kk, vv, 0, slots, hq)
+        outs.append(ops().paged_decode(qr, kk, vv, 0, tab, seq, overlap=overlap))
+    ops().check_device_errors(cuda)
+    assert torch.equal(outs[0], outs[1])
+    want = oatt.paged_decode(qr.cpu(), kk.cpu(), vv.cpu(), tables, lens, 0)
+    torch.testing.assert_close(outs[0].cpu().float(), want.float(), atol=2e-2, rtol=0)
