@@ -64,6 +64,13 @@ cudaError_t launch_after_trigger(void (*kernel)(KArgs...), dim3 grid, dim3 block
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Dependent launch of a kernel without dynamic shared memory; the error, if
+// any, is left for check_launch() (the runtime records it as the last error).
+template <typename... KArgs, typename... Args>
+void pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args&&... args) {
+  (void)launch_after_trigger(kernel, grid, block, 0, s, std::forward<Args>(args)...);
+}
+
 inline int dtype_size(int dtype) {
   switch (dtype) {
     case NIE_DTYPE_F32: return 4;

@@ -27,6 +27,8 @@ template <typename T, int THREADS>
 __global__ void __launch_bounds__(THREADS) add_rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ residual,
                                                                const T* __restrict__ weight, float eps, int hidden,
                                                                T* __restrict__ sum_out, T* __restrict__ out) {
+  pdl_wait();     // dependent launch: inputs come from the kernel before
+  pdl_trigger();  // and the kernel after may be staged now
   using N = Num<T>;
   const int64_t row = blockIdx.x;
   const T* xr = x + row * hidden;
@@ -78,6 +80,7 @@ __global__ void __launch_bounds__(256) rope_write_kernel(
     T* __restrict__ q_out, T* __restrict__ kc, T* __restrict__ vc, int64_t layer_off, int64_t total_slots,
     const int64_t* __restrict__ slots, int32_t* __restrict__ err) {
   using N = Num<T>;
+  pdl_wait();     // dependent launch: q/k/v come from the projection before
   pdl_trigger();  // the attention kernel after this one may start its prologue
   const int64_t t = blockIdx.x;
   const int half = d / 2;
@@ -121,6 +124,8 @@ __global__ void __launch_bounds__(256) rope_write_kernel(
 template <typename T>
 __global__ void silu_mul_kernel(const T* __restrict__ gate, int64_t g_stride, const T* __restrict__ up,
                                 int64_t u_stride, T* __restrict__ out, int64_t rows, int cols) {
+  pdl_wait();     // dependent launch: inputs come from the kernel before
+  pdl_trigger();  // and the kernel after may be staged now
   using N = Num<T>;
   const int64_t n = rows * cols;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += (int64_t)gridDim.x * blockDim.x) {
@@ -162,6 +167,8 @@ __global__ void __launch_bounds__(THREADS) add_rmsnorm_vec_kernel(const T* __res
                                                                   const T* __restrict__ residual,
                                                                   const T* __restrict__ weight, float eps, int hidden,
                                                                   T* __restrict__ sum_out, T* __restrict__ out) {
+  pdl_wait();     // dependent launch: inputs come from the kernel before
+  pdl_trigger();  // and the kernel after may be staged now
   using N = Num<T>;
   constexpr int V = Vec16<T>::N;
   const int64_t row = blockIdx.x;
@@ -211,6 +218,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) silu_mul_vec_kernel(const T* __restrict__ gate, int64_t g_stride,
                                                            const T* __restrict__ up, int64_t u_stride,
                                                            T* __restrict__ out, int cols) {
+  pdl_wait();     // dependent launch: inputs come from the kernel before
+  pdl_trigger();  // and the kernel after may be staged now
   using N = Num<T>;
   constexpr int V = Vec16<T>::N;
   const int64_t r = blockIdx.y;
@@ -236,6 +245,7 @@ __global__ void __launch_bounds__(256) rope_write_vec_kernel(
     T* __restrict__ q_out, T* __restrict__ kc, T* __restrict__ vc, int64_t layer_off, int64_t total_slots,
     const int64_t* __restrict__ slots, int32_t* __restrict__ err) {
   using N = Num<T>;
+  pdl_wait();     // dependent launch: q/k/v come from the projection before
   pdl_trigger();  // the attention kernel after this one may start its prologue
   constexpr int V = Vec16<T>::N;
   const int64_t t = blockIdx.x;
@@ -395,16 +405,16 @@ extern "C" int nie_add_rmsnorm(const void* x, const void* residual, const void* 
       aligned16(weight) && aligned16(sum_out) && aligned16(out)) {
     switch (dtype) {
       case NIE_DTYPE_BF16:
-        add_rmsnorm_vec_kernel<__nv_bfloat16, 256, 4><<<(unsigned)rows, 256, 0, s>>>(
+        pdl_launch(add_rmsnorm_vec_kernel<__nv_bfloat16, 256, 4>, dim3((unsigned)rows), dim3(256), s, 
             (const __nv_bfloat16*)x, (const __nv_bfloat16*)residual, (const __nv_bfloat16*)weight, eps, hidden,
             (__nv_bfloat16*)sum_out, (__nv_bfloat16*)out);
         break;
       case NIE_DTYPE_F32:
-        add_rmsnorm_vec_kernel<float, 256, 4><<<(unsigned)rows, 256, 0, s>>>(
+        pdl_launch(add_rmsnorm_vec_kernel<float, 256, 4>, dim3((unsigned)rows), dim3(256), s, 
             (const float*)x, (const float*)residual, (const float*)weight, eps, hidden, (float*)sum_out, (float*)out);
         break;
       default:
-        add_rmsnorm_vec_kernel<__half, 256, 4><<<(unsigned)rows, 256, 0, s>>>(
+        pdl_launch(add_rmsnorm_vec_kernel<__half, 256, 4>, dim3((unsigned)rows), dim3(256), s, 
             (const __half*)x, (const __half*)residual, (const __half*)weight, eps, hidden, (__half*)sum_out,
             (__half*)out);
         break;
@@ -413,17 +423,17 @@ extern "C" int nie_add_rmsnorm(const void* x, const void* residual, const void* 
   }
   switch (dtype) {
     case NIE_DTYPE_BF16:
-      add_rmsnorm_kernel<__nv_bfloat16, 256><<<(unsigned)rows, 256, 0, s>>>(
+      pdl_launch(add_rmsnorm_kernel<__nv_bfloat16, 256>, dim3((unsigned)rows), dim3(256), s, 
           (const __nv_bfloat16*)x, (const __nv_bfloat16*)residual, (const __nv_bfloat16*)weight, eps, hidden,
           (__nv_bfloat16*)sum_out, (__nv_bfloat16*)out);
       break;
     case NIE_DTYPE_F32:
-      add_rmsnorm_kernel<float, 256><<<(unsigned)rows, 256, 0, s>>>((const float*)x, (const float*)residual,
+      pdl_launch(add_rmsnorm_kernel<float, 256>, dim3((unsigned)rows), dim3(256), s, (const float*)x, (const float*)residual,
                                                                      (const float*)weight, eps, hidden,
                                                                      (float*)sum_out, (float*)out);
       break;
     case NIE_DTYPE_F16:
-      add_rmsnorm_kernel<__half, 256><<<(unsigned)rows, 256, 0, s>>>((const __half*)x, (const __half*)residual,
+      pdl_launch(add_rmsnorm_kernel<__half, 256>, dim3((unsigned)rows), dim3(256), s, (const __half*)x, (const __half*)residual,
                                                                       (const __half*)weight, eps, hidden,
                                                                       (__half*)sum_out, (__half*)out);
       break;
@@ -440,12 +450,12 @@ static void launch_rope_write(const void* q, int64_t qs, const void* k, int64_t 
   constexpr int V = Vec16<T>::N;
   if ((d / 2) % V == 0 && qs % V == 0 && ks % V == 0 && vs % V == 0 && aligned16(q) && aligned16(k) && aligned16(v) &&
       aligned16(sin) && aligned16(cos) && aligned16(q_out) && aligned16(kc) && aligned16(vc)) {
-    rope_write_vec_kernel<T><<<(unsigned)T_, 256, 0, s>>>((const T*)q, qs, (const T*)k, ks, (const T*)v, vs,
+    pdl_launch(rope_write_vec_kernel<T>, dim3((unsigned)T_), dim3(256), s, (const T*)q, qs, (const T*)k, ks, (const T*)v, vs,
                                                           (const T*)sin, (const T*)cos, hq, hkv, d, (T*)q_out, (T*)kc,
                                                           (T*)vc, layer_off, total_slots, slots, err);
     return;
   }
-  rope_write_kernel<T><<<(unsigned)T_, 256, 0, s>>>((const T*)q, qs, (const T*)k, ks, (const T*)v, vs, (const T*)sin,
+  pdl_launch(rope_write_kernel<T>, dim3((unsigned)T_), dim3(256), s, (const T*)q, qs, (const T*)k, ks, (const T*)v, vs, (const T*)sin,
                                                     (const T*)cos, hq, hkv, d, (T*)q_out, (T*)kc, (T*)vc, layer_off,
                                                     total_slots, slots, err);
 }
@@ -501,16 +511,16 @@ extern "C" int nie_silu_mul(const void* gate, int64_t gate_stride, const void* u
     const dim3 grid((unsigned)((cols / V + threads - 1) / threads), (unsigned)rows);
     switch (dtype) {
       case NIE_DTYPE_BF16:
-        silu_mul_vec_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>((const __nv_bfloat16*)gate, gate_stride,
+        pdl_launch(silu_mul_vec_kernel<__nv_bfloat16>, dim3(grid), dim3(threads), s, (const __nv_bfloat16*)gate, gate_stride,
                                                                     (const __nv_bfloat16*)up, up_stride,
                                                                     (__nv_bfloat16*)out, cols);
         break;
       case NIE_DTYPE_F32:
-        silu_mul_vec_kernel<float><<<grid, threads, 0, s>>>((const float*)gate, gate_stride, (const float*)up,
+        pdl_launch(silu_mul_vec_kernel<float>, dim3(grid), dim3(threads), s, (const float*)gate, gate_stride, (const float*)up,
                                                             up_stride, (float*)out, cols);
         break;
       default:
-        silu_mul_vec_kernel<__half><<<grid, threads, 0, s>>>((const __half*)gate, gate_stride, (const __half*)up,
+        pdl_launch(silu_mul_vec_kernel<__half>, dim3(grid), dim3(threads), s, (const __half*)gate, gate_stride, (const __half*)up,
                                                              up_stride, (__half*)out, cols);
         break;
     }
@@ -519,15 +529,15 @@ extern "C" int nie_silu_mul(const void* gate, int64_t gate_stride, const void* u
   const int64_t blocks = std::min<int64_t>((n + threads - 1) / threads, 148 * 16);
   switch (dtype) {
     case NIE_DTYPE_BF16:
-      silu_mul_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, s>>>(
+      pdl_launch(silu_mul_kernel<__nv_bfloat16>, dim3((unsigned)blocks), dim3(threads), s, 
           (const __nv_bfloat16*)gate, gate_stride, (const __nv_bfloat16*)up, up_stride, (__nv_bfloat16*)out, rows, cols);
       break;
     case NIE_DTYPE_F32:
-      silu_mul_kernel<float><<<(unsigned)blocks, threads, 0, s>>>((const float*)gate, gate_stride, (const float*)up,
+      pdl_launch(silu_mul_kernel<float>, dim3((unsigned)blocks), dim3(threads), s, (const float*)gate, gate_stride, (const float*)up,
                                                                   up_stride, (float*)out, rows, cols);
       break;
     case NIE_DTYPE_F16:
-      silu_mul_kernel<__half><<<(unsigned)blocks, threads, 0, s>>>((const __half*)gate, gate_stride,
+      pdl_launch(silu_mul_kernel<__half>, dim3((unsigned)blocks), dim3(threads), s, (const __half*)gate, gate_stride,
                                                                    (const __half*)up, up_stride, (__half*)out, rows,
                                                                    cols);
       break;

@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(kLnThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(dsm + kLnStages * Lay::kStageBytes + Lay::kRecvBytes);
   uint64_t* empty = full + kLnStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();  // the kernel after this one may be staged now
   const int cs = (int)cluster_nctarank(), rank = (int)cluster_ctarank();
   const int tile = (int)(blockIdx.x / (unsigned)cs);
   const int s0 = (int)((int64_t)a.ksteps * rank / cs), s1 = (int)((int64_t)a.ksteps * (rank + 1) / cs);
@@ -151,6 +152,10 @@ __global__ void __launch_bounds__(kLnThreads, 1)
       prefetch_tensormap(&wmap);
       prefetch_tensormap(&xmap);
       const uint64_t stream_once = l2_policy_evict_first();
+      // dependent launch: x (and y's memory) belong to the kernel before until it
+      // completes; every global access of this kernel follows this wait (the
+      // consumers only write y after their stages, loaded below, have landed)
+      pdl_wait();
       int k = 0;
       for (; k < steps; ++k) {
         const int st = k % kLnStages;
@@ -372,13 +377,15 @@ extern "C" int nie_linear(const void* x, int64_t ldx, const void* w, int64_t n, 
   cfg.blockDim = dim3(kLnThreads);
   cfg.dynamicSmemBytes = rows == 128 ? LnLayout<128>::kSmem : LnLayout<64>::kSmem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)cs;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = rows == 128 ? cudaLaunchKernelEx(&cfg, linear_stream_kernel<128>, wmap, xmap, la)
                               : cudaLaunchKernelEx(&cfg, linear_stream_kernel<64>, wmap, xmap, la);
   if (e != cudaSuccess) return fail(NIE_ERR_CUDA, "linear_stream_kernel launch: %s", cudaGetErrorString(e));
