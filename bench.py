@@ -328,7 +328,7 @@ def run_pd(args, dist_ctx, rank, local, device, world):
     value = len(host) * args.new_tokens * args.steps / elapsed
     e2e = None
     if not args.no_e2e:
-        e2e_steps = max(1, args.steps // 2)
+        e2e_steps = max(2, args.steps)
         e2e_s, (_, h2d, d2h) = time_pd(pd, e2e_steps, 0, dist_ctx, e2e=True)
         e2e = {"value": len(host) * args.new_tokens * e2e_steps / e2e_s, "unit": UNIT,
                "h2d_bytes_per_step": h2d // e2e_steps, "d2h_bytes_per_step": d2h // e2e_steps}
@@ -816,9 +816,9 @@ def main():
 
     e2e = None
     if not args.no_e2e:
-        e2e_s, h2d, d2h = time_e2e(model, cache, host_prompts, args.new_tokens, max(1, args.steps // 2), device)
+        e2e_s, h2d, d2h = time_e2e(model, cache, host_prompts, args.new_tokens, max(2, args.steps), device)
         e2e_s = max_over_ranks(dist_ctx, e2e_s, device)
-        e2e = {"value": args.requests * args.new_tokens * max(1, args.steps // 2) * world / e2e_s, "unit": UNIT,
+        e2e = {"value": args.requests * args.new_tokens * max(2, args.steps) * world / e2e_s, "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
     del cache

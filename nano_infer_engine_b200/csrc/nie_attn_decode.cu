@@ -412,6 +412,7 @@ __global__ void __launch_bounds__(512, 1)
 template <int CHUNK>
 __global__ void __launch_bounds__(kDecHD, CHUNK <= 8 ? 14 : 8) decode_combine_kernel(DecodeArgs a) {
   constexpr int kChunk = CHUNK;
+  pdl_trigger();  // the projection after the attention may be staged now (it waits for this grid)
   const int i = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int R = a.num_req;
   const int32_t* cum = a.cum_out;

@@ -50,8 +50,8 @@ std::pair<at::Tensor, at::Tensor> add_rmsnorm(const at::Tensor& x, const at::Ten
   return {residual ? (sum.defined() ? sum : at::Tensor()) : x, out};
 }
 
-// x @ w^T: decode-size bf16 batches of long-K matrices on nie_linear (the
-// choice the Python loop's ops.linear makes), everything else at::linear.
+// x @ w^T: decode-size bf16 batches with K >= N on nie_linear (the choice the
+// Python loop's ops.linear makes), everything else at::linear.
 struct Linear {
   bool enabled = false;
   int32_t* err = nullptr;
@@ -60,8 +60,8 @@ struct Linear {
 
   at::Tensor operator()(const at::Tensor& x, const at::Tensor& w) {
     const int64_t m = x.size(0), n = w.size(0), k = w.size(1);
-    // long-K matrices only (K >= 2N), where the cluster K split beats cuBLAS
-    if (enabled && m >= 1 && m <= 16 && k >= 2 * n && x.scalar_type() == at::kBFloat16 &&
+    // K >= N only (o_proj, down_proj), where the cluster K split beats cuBLAS
+    if (enabled && m >= 1 && m <= 16 && k >= n && x.scalar_type() == at::kBFloat16 &&
         w.scalar_type() == at::kBFloat16 &&
         x.stride(1) == 1 && w.is_contiguous() && x.size(1) == k) {
       at::Tensor y = at::empty({m, n}, x.options());

@@ -608,14 +608,15 @@ LINEAR_MAX_ROWS = 16
 def linear_eligible(x: torch.Tensor, weight: torch.Tensor) -> bool:
     """True when :func:`linear` runs ``x @ weight.T`` on the weight-streaming kernel.
 
-    Taken for long-K matrices (K >= 2N, e.g. down_proj), where the kernel's K
-    split over a cluster beats the library GEMM (measured 10.4 vs 12.8 us for
-    16 x 8192 x 2048 on B200); for K < 2N the library GEMM is as fast or faster.
+    Taken for K >= N (o_proj, down_proj), where the kernel's K split over a
+    cluster beats the library GEMM (B200, CUDA graphs, 16 rows: o_proj 4.6 vs
+    5.5 us, down_proj 9.6 vs 12.9 us); for K < N (q/k/v, gate/up) the library
+    GEMM is faster.
     """
     return (
         STREAM_LINEAR
         and weight.ndim == 2
-        and weight.shape[1] >= 2 * weight.shape[0]
+        and weight.shape[1] >= weight.shape[0]
         and x.is_cuda
         and x.dtype == torch.bfloat16
         and weight.dtype == torch.bfloat16

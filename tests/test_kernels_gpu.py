@@ -473,8 +473,8 @@ def test_stream_linear_matches_fp32_reference(cuda, m, n, k):
 
 
 def test_stream_linear_strided_rows_and_routing(cuda):
-    """x rows with a stride (a column slice) use the kernel; ops.linear routes long-K
-    matrices to it and everything else (more rows, K < 2N, ragged N) to torch."""
+    """x rows with a stride (a column slice) use the kernel; ops.linear routes K >= N
+    matrices to it and everything else (more rows, K < N, ragged N) to torch."""
     g = torch.Generator().manual_seed(1)
     big = torch.randn(9, 3072, generator=g).to(torch.bfloat16).to(cuda)
     x = big[:, 1024:3072]
@@ -487,8 +487,8 @@ def test_stream_linear_strided_rows_and_routing(cuda):
     x17 = torch.randn(17, 2048, generator=g).to(torch.bfloat16).to(cuda)
     assert not ops().linear_eligible(x17, w)
     assert torch.equal(ops().linear(x17, w), torch.nn.functional.linear(x17, w))
-    square = torch.randn(2048, 2048, generator=g).to(torch.bfloat16).to(cuda)
-    assert not ops().linear_eligible(x, square)
+    wide = torch.randn(4096, 2048, generator=g).to(torch.bfloat16).to(cuda)
+    assert not ops().linear_eligible(x, wide)
     w100 = torch.randn(100, 2048, generator=g).to(torch.bfloat16).to(cuda)
     assert not ops().linear_eligible(x, w100)
     ops().check_device_errors(cuda)
