@@ -369,6 +369,18 @@ int nie_linear(const void* x, int64_t ldx, const void* w, int64_t n, int64_t k,
                int64_t m, void* y, int64_t ldy, int32_t dtype,
                int32_t* err_flag, void* stream);
 
+/*
+ * nie_linear_overlapped: nie_linear that starts streaming w while the kernel
+ * issued just before it on `stream` is still running (x is read only after
+ * that kernel completes).  Precondition: that immediately preceding kernel
+ * must NOT write w (weights are normally written long before; the engine calls
+ * this right after the attention combine or SiLU * up kernel).  Same
+ * arguments, results and errors as nie_linear.
+ */
+int nie_linear_overlapped(const void* x, int64_t ldx, const void* w, int64_t n,
+                          int64_t k, int64_t m, void* y, int64_t ldy,
+                          int32_t dtype, int32_t* err_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

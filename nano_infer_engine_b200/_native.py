@@ -95,6 +95,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int32, c_void_p, c_void_p],
     ),
+    "nie_linear_overlapped": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int32, c_void_p, c_void_p],
+    ),
     "nie_varlen_workspace_size": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "nie_varlen_attention": (
         c_int,

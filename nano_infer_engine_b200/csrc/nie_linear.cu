@@ -63,6 +63,7 @@ struct LinearArgs {
   int m;
   int ksteps;  // k-steps per n-tile (K / 64)
   int32_t* err;
+  int early_weights;  // issue the first ring of weight loads before waiting for the previous kernel
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -152,11 +153,23 @@ __global__ void __launch_bounds__(kLnThreads, 1)
       prefetch_tensormap(&wmap);
       prefetch_tensormap(&xmap);
       const uint64_t stream_once = l2_policy_evict_first();
-      // dependent launch: x (and y's memory) belong to the kernel before until it
-      // completes; every global access of this kernel follows this wait (the
-      // consumers only write y after their stages, loaded below, have landed)
-      pdl_wait();
+      // Dependent launch: x (and y's memory) belong to the kernel before until it
+      // completes, so x is loaded only after this wait (the consumers write y
+      // only after their stages, x included, have landed).  With early_weights
+      // the caller guarantees that kernel does not write w: the first ring of
+      // weight tiles is already streaming while it finishes.
       int k = 0;
+      if (a.early_weights) {
+        for (; k < steps && k < kLnStages; ++k) {
+          mbar_arrive_expect_tx(&full[k], Lay::kStageBytes);
+          tma_load_2d_hint(dsm + k * Lay::kStageBytes, &wmap, &full[k], (s0 + k) * kLnK, tile * ROWS, stream_once);
+        }
+        pdl_wait();
+        for (int j = 0; j < k; ++j)
+          tma_load_2d(dsm + j * Lay::kStageBytes + Lay::kWBytes, &xmap, &full[j], (s0 + j) * kLnK, 0);
+      } else {
+        pdl_wait();
+      }
       for (; k < steps; ++k) {
         const int st = k % kLnStages;
         if (k >= kLnStages && !mbar_wait_bounded(&empty[st], (uint32_t)((k / kLnStages) - 1) & 1u, kLnWaitProbes)) {
@@ -301,8 +314,8 @@ int opt_in_both() {
 
 using namespace nie;
 
-extern "C" int nie_linear(const void* x, int64_t ldx, const void* w, int64_t n, int64_t k, int64_t m, void* y,
-                          int64_t ldy, int32_t dtype, int32_t* err_flag, void* stream) {
+static int linear_impl(const void* x, int64_t ldx, const void* w, int64_t n, int64_t k, int64_t m, void* y,
+                       int64_t ldy, int32_t dtype, int32_t* err_flag, void* stream, bool early_weights) {
   NIE_REQUIRE(x && w && y, "null pointer argument");
   NIE_REQUIRE(m >= 0 && n > 0 && k > 0, "bad shape m=%lld n=%lld k=%lld", (long long)m, (long long)n, (long long)k);
   if (dtype != NIE_DTYPE_BF16 || m > kLnXRows || n % 64 != 0 || k % kLnK != 0 ||
@@ -372,6 +385,7 @@ extern "C" int nie_linear(const void* x, int64_t ldx, const void* w, int64_t n, 
   la.m = (int)m;
   la.ksteps = ksteps;
   la.err = err_flag;
+  la.early_weights = early_weights ? 1 : 0;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(tiles * cs));
   cfg.blockDim = dim3(kLnThreads);
@@ -390,4 +404,14 @@ extern "C" int nie_linear(const void* x, int64_t ldx, const void* w, int64_t n, 
                               : cudaLaunchKernelEx(&cfg, linear_stream_kernel<64>, wmap, xmap, la);
   if (e != cudaSuccess) return fail(NIE_ERR_CUDA, "linear_stream_kernel launch: %s", cudaGetErrorString(e));
   return check_launch("linear_stream_kernel");
+}
+
+extern "C" int nie_linear(const void* x, int64_t ldx, const void* w, int64_t n, int64_t k, int64_t m, void* y,
+                          int64_t ldy, int32_t dtype, int32_t* err_flag, void* stream) {
+  return linear_impl(x, ldx, w, n, k, m, y, ldy, dtype, err_flag, stream, false);
+}
+
+extern "C" int nie_linear_overlapped(const void* x, int64_t ldx, const void* w, int64_t n, int64_t k, int64_t m,
+                                     void* y, int64_t ldy, int32_t dtype, int32_t* err_flag, void* stream) {
+  return linear_impl(x, ldx, w, n, k, m, y, ldy, dtype, err_flag, stream, true);
 }

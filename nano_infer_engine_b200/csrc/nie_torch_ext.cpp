@@ -58,15 +58,16 @@ struct Linear {
   void* stream = nullptr;
   int64_t launches = 0;
 
-  at::Tensor operator()(const at::Tensor& x, const at::Tensor& w) {
+  // overlap: the kernel that produced x (issued just before) does not write w
+  at::Tensor operator()(const at::Tensor& x, const at::Tensor& w, bool overlap = false) {
     const int64_t m = x.size(0), n = w.size(0), k = w.size(1);
     // K >= N only (o_proj, down_proj), where the cluster K split beats cuBLAS
     if (enabled && m >= 1 && m <= 16 && k >= n && x.scalar_type() == at::kBFloat16 &&
         w.scalar_type() == at::kBFloat16 &&
         x.stride(1) == 1 && w.is_contiguous() && x.size(1) == k) {
       at::Tensor y = at::empty({m, n}, x.options());
-      const int st =
-          nie_linear(x.data_ptr(), x.stride(0), w.data_ptr(), n, k, m, y.data_ptr(), n, NIE_DTYPE_BF16, err, stream);
+      const int st = (overlap ? nie_linear_overlapped : nie_linear)(x.data_ptr(), x.stride(0), w.data_ptr(), n, k,
+                                                                    m, y.data_ptr(), n, NIE_DTYPE_BF16, err, stream);
       if (st == NIE_OK) {
         ++launches;
         return y;
@@ -175,7 +176,7 @@ std::tuple<at::Tensor, int64_t> run_layers(
             "nie_varlen_attention");
       launches += var_bytes ? 2 : 1;
     }
-    at::Tensor attn = linear(att.view({T, hidden}), o_w);
+    at::Tensor attn = linear(att.view({T, hidden}), o_w, /*overlap=*/true);  // after the attention kernels
     // h = attn + residual, normed2 = post-norm(h)
     auto [h, normed2] = add_rmsnorm(attn, &residual, post_w, eps[2 * li + 1], true, stream);
     ++launches;
@@ -186,7 +187,7 @@ std::tuple<at::Tensor, int64_t> run_layers(
                        (int32_t)inner, dt, stream),
           "nie_silu_mul");
     ++launches;
-    at::Tensor mlp = linear(act, down_w);
+    at::Tensor mlp = linear(act, down_w, /*overlap=*/true);  // after SiLU * up
     if (li + 1 < n_layers) {
       auto [sum, nxt] = add_rmsnorm(mlp, &h, weights[6 * (li + 1)], eps[2 * (li + 1)], true, stream);
       ++launches;

@@ -38,13 +38,17 @@ def fused_weight(module: nn.Module, names: tuple[str, ...], attr: str) -> torch.
     return buf
 
 
-def apply_linear(module: nn.Linear, x: torch.Tensor) -> torch.Tensor:
-    """``module(x)`` without nn.Module call overhead when no hook is registered."""
+def apply_linear(module: nn.Linear, x: torch.Tensor, *, overlap: bool = False) -> torch.Tensor:
+    """``module(x)`` without nn.Module call overhead when no hook is registered.
+
+    ``overlap``: the kernel that produced ``x`` (issued just before) does not
+    write the weights, so a weight-streaming GEMM may start loading them early.
+    """
     if (module._forward_hooks or module._forward_pre_hooks or nn.modules.module._global_forward_hooks
             or nn.modules.module._global_forward_pre_hooks):
         return module(x)
     params = module._parameters
-    return ops.linear(x, params["weight"], params["bias"])
+    return ops.linear(x, params["weight"], params["bias"], overlap=overlap)
 
 
 def fuse_linears(module: nn.Module, names: tuple[str, ...], attr: str) -> bool:
@@ -167,7 +171,8 @@ class GroupedQueryAttention(nn.Module):
                 num_requests=meta.num_prefill,
                 max_seq_len=meta.max_seq_len,
             )
-        return apply_linear(self.o_proj, out.view(T, self.hidden_size))
+        # out comes from the attention (or its combine) kernel just before: it does not write weights
+        return apply_linear(self.o_proj, out.view(T, self.hidden_size), overlap=True)
 
     # ---------------------------------------------------- reference entry
     def forward(

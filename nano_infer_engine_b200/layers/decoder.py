@@ -51,7 +51,8 @@ class Llama3Decoder(nn.Module):
         else:
             gate = self.ffn.gate_proj(normed2)
             up = self.ffn.up_proj(normed2)
-        return apply_linear(self.ffn.down_proj, ops.silu_mul(gate, up)), h
+        # the SiLU * up kernel just before does not write weights
+        return apply_linear(self.ffn.down_proj, ops.silu_mul(gate, up), overlap=True), h
 
     def fuse_projections(self) -> bool:
         """Single-buffer q/k/v and gate/up weights (see ``fuse_linears``)."""

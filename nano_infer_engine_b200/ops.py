@@ -634,22 +634,29 @@ def linear_eligible(x: torch.Tensor, weight: torch.Tensor) -> bool:
     )
 
 
-def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
-    """``torch.nn.functional.linear(x, weight, bias)``; decode-size bf16 batches of long-K
-    matrices stream the weights through ``nie_linear`` (fp32 accumulation, one rounding)."""
+def linear(
+    x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *, overlap: bool = False
+) -> torch.Tensor:
+    """``torch.nn.functional.linear(x, weight, bias)``; decode-size bf16 batches with K >= N
+    stream the weights through ``nie_linear`` (fp32 accumulation, one rounding).  ``overlap``:
+    see :func:`linear_stream`."""
     if bias is not None or not linear_eligible(x, weight):
         return torch.nn.functional.linear(x, weight, bias)
-    return linear_stream(x, weight)
+    return linear_stream(x, weight, overlap=overlap)
 
 
-def linear_stream(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+def linear_stream(x: torch.Tensor, weight: torch.Tensor, *, overlap: bool = False) -> torch.Tensor:
     """``x @ weight.T`` on ``nie_linear`` for any shape it takes (``x`` bf16 [m <= 16, k],
-    ``weight`` contiguous bf16 [n, k], n and k multiples of 64); torch otherwise."""
+    ``weight`` contiguous bf16 [n, k], n and k multiples of 64); torch otherwise.
+
+    ``overlap`` (``nie_linear_overlapped``) starts loading the weights before the previous
+    kernel on the stream has finished: that kernel must not write ``weight``.
+    """
     _require_cuda(x, weight)
     n, k = weight.shape
     m = x.shape[0]
     y = torch.empty((m, n), dtype=x.dtype, device=x.device)
-    status = lib.nie_linear(
+    status = (lib.nie_linear_overlapped if overlap else lib.nie_linear)(
         x.data_ptr(), x.stride(0), weight.data_ptr(), n, k, m, y.data_ptr(), n, NIE_DTYPE_BF16,
         error_flag(x.device).data_ptr(), _stream(x),
     )

@@ -526,3 +526,21 @@ def test_overlapped_decode_sees_the_rope_kernel_writes(cuda):
     assert torch.equal(outs[0], outs[1])
     want = oatt.paged_decode(qr.cpu(), kk.cpu(), vv.cpu(), tables, lens, 0)
     torch.testing.assert_close(outs[0].cpu().float(), want.float(), atol=2e-2, rtol=0)
+
+
+@pytest.mark.parametrize("n,k", [(2048, 8192), (2048, 2048), (256, 64 * 40)])
+def test_overlapped_linear_after_the_kernel_that_writes_x(cuda, n, k):
+    """nie_linear_overlapped right after SiLU * up (the kernel that writes x): the weights stream
+    early, x is read after that kernel; the result equals nie_linear's bit for bit."""
+    g = torch.Generator().manual_seed(n + k)
+    gate = torch.randn(16, k, generator=g).to(torch.bfloat16).to(cuda)
+    up = torch.randn(16, k, generator=g).to(torch.bfloat16).to(cuda)
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).to(torch.bfloat16).to(cuda)
+    outs = []
+    for overlap in (True, False):
+        torch.cuda.synchronize()
+        act = ops().silu_mul(gate, up)
+        outs.append(ops().linear_stream(act, w, overlap=overlap))
+    ops().check_device_errors(cuda)
+    assert torch.equal(outs[0], outs[1])
+    torch.testing.assert_close(outs[0].float(), act.float() @ w.float().T, atol=2e-3, rtol=2 ** -7)
