@@ -181,3 +181,32 @@ def test_cpu_cache_data_ops_fail_loudly():
     c.ensure_capacity("a", 2)
     with pytest.raises(RuntimeError, match="require a CUDA cache|require CUDA tensors"):
         c.write(0, "a", 0, torch.zeros(2, 2, 4), torch.zeros(2, 2, 4))
+
+
+def test_layer_loop_eligibility_follows_the_python_loop_checks():
+    """The C++ layer loop runs only when the Python loop's fused-weight, hook and bias checks hold."""
+    from torch import nn
+
+    from nano_infer_engine_b200.models.llama import LlamaConfig, build_random_llama
+
+    cfg = LlamaConfig(vocab_size=64, hidden_size=128, mlp_inner_size=256, num_layers=2, q_head_num=2,
+                      kv_head_num=1, max_seq_len=256)
+    model = build_random_llama(cfg, 3, 0.02, torch.bfloat16, "cpu")
+    model._ensure_fused()
+    args = model._layer_loop_args(torch.bfloat16)
+    assert args is not None
+    weights, eps = args
+    assert len(weights) == 6 * cfg.num_layers and len(eps) == 2 * cfg.num_layers
+    assert model._layer_loop_args(torch.float32) is None  # dtype mismatch
+    o_proj = model.decoders[1].attn.o_proj
+    handle = o_proj.register_forward_hook(lambda *a: None)
+    assert model._layer_loop_args(torch.bfloat16) is None
+    handle.remove()
+    assert model._layer_loop_args(torch.bfloat16) is not None
+    down = model.decoders[0].ffn.down_proj
+    down.bias = nn.Parameter(torch.zeros(down.out_features, dtype=torch.bfloat16))
+    assert model._layer_loop_args(torch.bfloat16) is None
+    down.bias = None
+    attn = model.decoders[0].attn
+    attn.k_proj.weight = nn.Parameter(attn.k_proj.weight.detach().clone())  # no longer a view of the fused buffer
+    assert model._layer_loop_args(torch.bfloat16) is None

@@ -200,3 +200,61 @@ def test_prefill_chunks_contract_with_foreign_models():
         paged_prefill(model, (torch.tensor([[1]]),), _cache(4), ("a", "b"))
     with pytest.raises(ValueError, match="sequence IDs must be unique"):
         paged_prefill(model, (torch.tensor([[1]]), torch.tensor([[2]])), _cache(4), ("a", "a"))
+
+
+def test_retire_by_count_defers_the_token_appends():
+    """Without token values (no EOS configured) retirement goes by count and the caller appends later."""
+    cache = _cache(32, block_size=2)
+    s = ContinuousBatchingScheduler(ScriptedModel(), GenerationConfig(max_new_tokens=2), cache, 2)
+    reqs = [PagedRequest(sequence_id=sid, prompt=torch.tensor([[1, 2]])) for sid in ("a", "b")]
+    reqs[1].generated_tokens = 1
+    done: list = []
+    keep = s._retire(reqs, None, done)
+    assert keep == [0] and done == [reqs[1]]
+    assert [r.generated_tokens for r in reqs] == [1, 2]
+    assert all(r.sequence.shape[1] == 2 for r in reqs)  # nothing appended yet
+    s_eos = ContinuousBatchingScheduler(ScriptedModel(), GenerationConfig(max_new_tokens=2, eos_token_id=3),
+                                        _cache(32, block_size=2), 2)
+    with pytest.raises(ValueError, match="EOS"):
+        s_eos._retire(reqs, None, [])
+
+
+@pytest.mark.parametrize("chunk", [4, None])
+def test_deferred_token_read_keeps_plans_tokens_and_events(chunk, monkeypatch):
+    """The deferred path (next forward queued before the sampled values are read, used on CUDA)
+    gives the same ragged calls, tokens, events and block accounting as reading them first."""
+    from nano_infer_engine_b200.generation import scheduler as sched_mod
+
+    class FakePending(sched_mod._PendingTokens):
+        def __init__(self, tokens):  # the values are already on the host here
+            self.tokens = tokens.reshape(-1).tolist()
+
+        def values(self):
+            return self.tokens
+
+    def run(deferred):
+        if deferred:
+            original = sched_mod.ContinuousBatchingScheduler._sample
+
+            def sample(self, requests, *, defer=False):
+                next_tokens, ids = original(self, requests)
+                return (next_tokens, FakePending(next_tokens)) if defer and requests else (next_tokens, ids)
+
+            monkeypatch.setattr(sched_mod.ContinuousBatchingScheduler, "_sample", sample)
+        else:
+            monkeypatch.undo()
+        model = ScriptedModel({"a": (3, 5, 6, 1), "b": (2, 4), "c": (7,)})
+        cache = _cache(64, block_size=2)
+        s = ContinuousBatchingScheduler(model, GenerationConfig(max_new_tokens=4, prefill_chunk_size=chunk),
+                                        cache, 2)
+        reqs = [s.add_request(sid, torch.tensor([p])) for sid, p in (("a", [1, 2, 3]), ("b", [4, 5]), ("c", [6]))]
+        events = []
+        while s.has_work:
+            out = s.step()
+            events.append((out.token_events, tuple(r.sequence_id for r in out.terminal_requests)))
+        seqs = [r.sequence[0].tolist() for r in reqs]
+        return seqs, events, model.ragged_calls, model.decode_calls, cache.allocator.allocated_block_count
+
+    sync = run(False)
+    deferred = run(True)
+    assert deferred == sync
