@@ -44,3 +44,24 @@ def test_invalid_arguments_fail_before_any_launch():
     assert rc == _native.NIE_ERR_INVALID
     rc = lib.nie_write_kv(1, 1, 4, 1, 1, 7, 0, 1, 8, 16, 8, 64, 1, None, None)
     assert rc == _native.NIE_ERR_INVALID and b"dtype" in lib.nie_last_error()
+
+
+def test_new_entry_points_validate_before_any_launch():
+    """nie_linear(_overlapped) and nie_paged_decode_overlapped reject bad arguments on the host."""
+    lib = _native.lib
+    for fn in (lib.nie_linear, lib.nie_linear_overlapped):
+        assert fn(None, 64, None, 128, 64, 1, None, 128, _native.NIE_DTYPE_BF16, None, None) == _native.NIE_ERR_INVALID
+        # shapes the weight-streaming kernel does not take come back as UNSUPPORTED, so
+        # a caller can fall back to a library GEMM (no pointer is dereferenced)
+        fake = 1 << 20
+        assert fn(fake, 64, fake, 128, 64, 17, fake, 128, _native.NIE_DTYPE_BF16, None, None) == \
+            _native.NIE_ERR_UNSUPPORTED  # 17 rows
+        assert fn(fake, 64, fake, 128, 64, 4, fake, 128, _native.NIE_DTYPE_F32, None, None) == \
+            _native.NIE_ERR_UNSUPPORTED  # fp32
+        assert fn(fake, 64, fake, 100, 64, 4, fake, 100, _native.NIE_DTYPE_BF16, None, None) == \
+            _native.NIE_ERR_UNSUPPORTED  # n not a multiple of 64
+        assert fn(fake + 2, 64, fake, 128, 64, 4, fake, 128, _native.NIE_DTYPE_BF16, None, None) == \
+            _native.NIE_ERR_UNSUPPORTED  # x not 16-byte aligned
+    rc = lib.nie_paged_decode_overlapped(None, 0, None, 0, None, None, 1, 0, 1, 8, 16, 8, 64, 32, None, 1,
+                                         None, None, None, None, 1, 0.125, None, 0, None, None)
+    assert rc == _native.NIE_ERR_INVALID and b"null pointer" in lib.nie_last_error()
