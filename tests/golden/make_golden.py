@@ -1,9 +1,9 @@
 """Generate the golden fixtures by running the REFERENCE implementation.
 
-Run in a container that has the reference checkout (read-only) at
-$NIE_REFERENCE_SRC (default /root/reference/src):
+Run where the reference checkout is available, with NIE_REFERENCE_SRC set
+to its `src` directory (the one holding the `nano_infer_engine` package):
 
-    python tests/golden/make_golden.py
+    NIE_REFERENCE_SRC=<reference>/src python tests/golden/make_golden.py
 
 It imports the reference package ``nano_infer_engine`` and this repository's
 seeded recipes (tests/golden/recipes.py) and writes only reference OUTPUTS:
@@ -22,7 +22,9 @@ import torch
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
 sys.path.insert(0, str(HERE.parent.parent))
-sys.path.insert(0, os.environ.get("NIE_REFERENCE_SRC", "/root/reference/src"))
+if "NIE_REFERENCE_SRC" not in os.environ:
+    raise SystemExit("set NIE_REFERENCE_SRC to the reference checkout's src directory")
+sys.path.insert(0, os.environ["NIE_REFERENCE_SRC"])
 
 import recipes  # noqa: E402
 from nano_infer_engine.generation.config import GenerationConfig  # noqa: E402
