@@ -62,6 +62,8 @@ def test_new_entry_points_validate_before_any_launch():
             _native.NIE_ERR_UNSUPPORTED  # n not a multiple of 64
         assert fn(fake + 2, 64, fake, 128, 64, 4, fake, 128, _native.NIE_DTYPE_BF16, None, None) == \
             _native.NIE_ERR_UNSUPPORTED  # x not 16-byte aligned
+        # an empty batch is done before any device call
+        assert fn(fake, 64, fake, 128, 64, 0, fake, 128, _native.NIE_DTYPE_BF16, None, None) == _native.NIE_OK
     rc = lib.nie_paged_decode_overlapped(None, 0, None, 0, None, None, 1, 0, 1, 8, 16, 8, 64, 32, None, 1,
                                          None, None, None, None, 1, 0.125, None, 0, None, None)
     assert rc == _native.NIE_ERR_INVALID and b"null pointer" in lib.nie_last_error()
