@@ -303,10 +303,19 @@ int pick_cluster(int dev, int tiles, int ksteps, int sms) {
   return 0;
 }
 
-int opt_in_both() {
+// Per-device set-up on the first call: the shared-memory opt-in of both
+// kernel instances and the whole resident-cluster table, so that later calls
+// (a new shape, or a call inside a CUDA-graph capture) only read the table.
+int opt_in_both(int dev) {
   int rc = opt_in_smem(kSmemLinear, (const void*)linear_stream_kernel<128>, LnLayout<128>::kSmem);
   if (rc != NIE_OK) return rc;
-  return opt_in_smem(kSmemLinear64, (const void*)linear_stream_kernel<64>, LnLayout<64>::kSmem);
+  rc = opt_in_smem(kSmemLinear64, (const void*)linear_stream_kernel<64>, LnLayout<64>::kSmem);
+  if (rc != NIE_OK) return rc;
+  for (int c = 1; c <= kLnMaxCluster; ++c) {
+    max_active_clusters<128>(dev, c);
+    max_active_clusters<64>(dev, c);
+  }
+  return NIE_OK;
 }
 
 }  // namespace
@@ -337,7 +346,7 @@ static int linear_impl(const void* x, int64_t ldx, const void* w, int64_t n, int
   int rows = 0, cs = 0;
   {
     std::lock_guard<std::mutex> lk(g_ln_mu);
-    const int rc = opt_in_both();
+    const int rc = opt_in_both(dev);
     if (rc != NIE_OK) return rc;
     const int c128 = n % 128 == 0 ? pick_cluster<128>(dev, (int)(n / 128), ksteps, sms) : 0;
     const int c64 = pick_cluster<64>(dev, (int)(n / 64), ksteps, sms);
