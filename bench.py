@@ -48,6 +48,17 @@ SEED = 1234
 
 
 # ------------------------------------------------------------------ helpers
+def headline_config(args, world):
+    """The N=1 / replica workload description, shared verbatim by both arms."""
+    return {
+        "workload": "config2: Llama-3.2-1B shape, 16 requests, prompts U[128,2048], 256 greedy new "
+                    "tokens, prefill chunk 128, <=512 prefill tokens/step, block 16, max_model_len 29600",
+        "global_batch": args.requests * world,
+        "parallelism": f"replicas x{world}",
+        "l2": "inputs larger than L2 (2.47 GB of weights streamed per decode step)",
+    }
+
+
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -646,15 +657,15 @@ def cpu_sample(prompts, model_cpu_state, threads):
     one 16-token decode step at the workload's context lengths; extrapolated to the
     whole run (ceil(sum(prompt)/512) prefill steps + (new_tokens) decode steps)."""
     from oracle.engine import OracleCache, OracleLlama
+    from oracle.weights import LLAMA_1B
 
     torch.set_num_threads(threads)
-    cfg = llama_1b_config()
-    config = dict(hidden_size=cfg.hidden_size, q_head_num=cfg.q_head_num, kv_head_num=cfg.kv_head_num,
-                  num_layers=cfg.num_layers, norm_eps=cfg.norm_eps, rope_theta=cfg.rope_theta, rope_type="llama3")
-    model = OracleLlama(model_cpu_state, config)
+    cfg = LLAMA_1B
+    model = OracleLlama(model_cpu_state, cfg)
     lens = [p.shape[1] for p in prompts]
     blocks = sum(-(-(n + 1) // 16) for n in lens) + 64
-    cache = OracleCache(blocks, 16, cfg.num_layers, 8, 64, torch.bfloat16)
+    hd = cfg["hidden_size"] // cfg["q_head_num"]
+    cache = OracleCache(blocks, 16, cfg["num_layers"], cfg["kv_head_num"], hd, torch.bfloat16)
     ids = [f"r{i}" for i in range(len(prompts))]
     # contexts as if each prompt were already cached (values do not affect time)
     for s, n in zip(ids, lens):
@@ -690,10 +701,11 @@ def cpu_baseline(prompts, new_tokens, state):
 
 
 def cpu_state_for_oracle():
-    from nano_infer_engine_b200.models.llama import build_random_llama
+    """The engine's random-init weights, rebuilt by the oracle (no product import: the
+    reference arm must not load this package or its native library)."""
+    from oracle.weights import LLAMA_1B, random_llama_state
 
-    model = build_random_llama(llama_1b_config(), SEED, 0.02, torch.bfloat16, "cpu")
-    return dict(model.state_dict())
+    return random_llama_state(LLAMA_1B, SEED, 0.02, torch.bfloat16)
 
 
 # --------------------------------------------------------------- dist
@@ -741,6 +753,10 @@ def run_reference(args):
         values.append(len(prompts) * args.new_tokens / (n_pf * t_pf + args.new_tokens * t_dec))
     wall = time.perf_counter() - t_start
     value = statistics.median(values)
+    sample = ("oracle port of the reference forward (torch on the host cores, no product code loaded); "
+              "each step times one 512-token prefill step (4 chunks of 128) and one 16-request decode step "
+              "at the workload's prompt contexts and extrapolates to the whole generation "
+              f"(ceil(sum(prompt)/512) prefill + {args.new_tokens} decode steps); median over steps")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -754,11 +770,10 @@ def run_reference(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded prompts, random-init weights std 0.02)",
-        "config": {"workload": "config2: Llama-3.2-1B, 16 req, prompts U[128,2048], 256 new, chunk 128/512",
-                   "sample": "per step: one 512-token prefill step + one decode step, extrapolated"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": "oracle port of the reference forward on the host cores"},
+        "data": "synthetic (seeded prompts, random-init weights N(0, 0.02))",
+        "config": headline_config(args, 1),
+        "sample": sample,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -856,13 +871,7 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded prompts, random-init weights N(0, 0.02))",
-            "config": {
-                "workload": "config2: Llama-3.2-1B shape, 16 requests, prompts U[128,2048], 256 greedy new "
-                            "tokens, prefill chunk 128, <=512 prefill tokens/step, block 16, max_model_len 29600",
-                "global_batch": args.requests * world,
-                "parallelism": f"replicas x{world}",
-                "l2": "inputs larger than L2 (2.47 GB of weights streamed per decode step)",
-            },
+            "config": headline_config(args, world),
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
