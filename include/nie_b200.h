@@ -7,11 +7,11 @@
  * JNI alike.  All pointers are DEVICE pointers unless stated otherwise.
  *
  * Cache layout (identical to the reference's PagedKVCache storage,
- * nano_infer_engine/paged_cache.py:131-139):
+ * nano_infer_engine/paged_cache.py:71-79):
  *     key_cache / value_cache : [num_layers, num_blocks, block_size,
  *                                kv_heads, head_dim], contiguous
  * A "slot" is block_id * block_size + offset_in_block
- * (nano_infer_engine/paged_cache.py:313-322).
+ * (nano_infer_engine/paged_cache.py:240-262, used by write at :311-322).
  *
  * Return value: NIE_OK (0) or an NIE_ERR_* code; nie_last_error() gives the
  * message of the last failure on the calling thread.  Launches are
@@ -60,9 +60,9 @@ int nie_device_sm_count(int device);
  * (a) Ragged batch packing.
  * Replaces the host-side packing of the reference:
  *   query_start_loc      nano_infer_engine/generation/paged_prefill.py:132-143
- *   position ids         nano_infer_engine/layers/attention.py:539-550
+ *   position ids         nano_infer_engine/layers/attention.py:363-376
  *   context lengths      nano_infer_engine/models/llama.py:364-369
- *   slot resolution      nano_infer_engine/paged_cache.py:300-322
+ *   slot resolution      nano_infer_engine/paged_cache.py:240-262, 306-322
  *   last-token rows      nano_infer_engine/generation/paged_prefill.py:154
  *
  * plan is int32 [3, num_requests] (device): row 0 = block-table row, row 1 =
@@ -93,7 +93,7 @@ int nie_pack_ragged(const int32_t* plan, int32_t num_requests, int64_t num_token
 
 /*
  * (b) Paged KV slot write.
- * Replaces PagedKVCache.write (nano_infer_engine/paged_cache.py:324-382):
+ * Replaces PagedKVCache.write (nano_infer_engine/paged_cache.py:264-322):
  * key_cache[layer, slot / bs, slot % bs] = keys[t] (and values) for every t
  * with slot_mapping[t] >= 0.  keys/values are contiguous [T, kv_heads,
  * head_dim] of `dtype`; the copy is bit-exact.
@@ -106,7 +106,7 @@ int nie_write_kv(const void* keys, const void* values, int64_t num_tokens,
 
 /*
  * Paged KV gather into contiguous [T, kv_heads, head_dim] tensors.
- * Replaces PagedKVCache.gather (nano_infer_engine/paged_cache.py:384-422):
+ * Replaces PagedKVCache.gather (nano_infer_engine/paged_cache.py:324-362):
  * out[t] = cache[layer, table[t / bs], t % bs] for t in [0, num_tokens).
  * block_table is the sequence's int32 row (logical block order).
  */
@@ -119,13 +119,13 @@ int nie_gather_kv(const void* key_cache, const void* value_cache, int32_t dtype,
 /*
  * (e) Block copy between two paged pools (same or peer device).
  * Replaces PagedKVCache.export_sequence / import_sequence
- * (nano_infer_engine/paged_cache.py:205-298) and the per-block cross-device
+ * (nano_infer_engine/paged_cache.py:145-238) and the per-block cross-device
  * copy_ of the P/D handoff (nano_infer_engine/generation/pd_scheduler.py:
- * 253-262).  For every layer l and logical block j < num_copy_blocks:
+ * 144-145 into paged_cache.py:228-234).  For every layer l and logical block j < num_copy_blocks:
  *   dst[l, dst_blocks[j]] = src[l, src_blocks[j]]
  * and, when tail_valid_tokens in (0, block_size), token rows
  * [tail_valid_tokens, block_size) of the LAST copied block are written as
- * zeros (the zeroed export tail, paged_cache.py:225-229).  src_blocks or
+ * zeros (the zeroed export tail, paged_cache.py:165-169).  src_blocks or
  * dst_blocks may be NULL meaning the identity (j), which lets a dense
  * [L, n, bs, H, D] transfer tensor act as either side.  The kernel runs on
  * the stream's device; a peer pointer (after nie_enable_peer_access) makes it
@@ -145,7 +145,7 @@ int nie_enable_peer_access(int device, int peer_device);
 /*
  * CUDA IPC for prefill/decode processes (one process per GPU).  The
  * reference moves KV between devices inside one process
- * (paged_cache.py:288-294); with a process per GPU the decode process maps
+ * (generation/pd_scheduler.py:144-145, paged_cache.py:228-234); with a process per GPU the decode process maps
  * the prefill process's pool and nie_copy_blocks pulls blocks over NVLink.
  * nie_ipc_export writes the 64-byte handle of the allocation that contains
  * `ptr` and ptr's offset in it; nie_ipc_import (in another process, on the
@@ -193,10 +193,15 @@ int nie_paged_decode(const void* q, int64_t q_row_stride, void* out,
  * (block-table walk, barrier setup) while the kernel issued just before it on
  * `stream` is still running; it waits for that kernel before reading q or the
  * caches.  Precondition: the block tables, table rows, seq_lens, q_rows and
- * the request list must NOT be written by that immediately preceding kernel
- * (the engine writes them in its packing kernel, many kernels earlier; q and
- * the new cache rows come from the RoPE + KV write right before).  Same
- * arguments, results and errors as nie_paged_decode.
+ * the request list must be complete before the most recent kernel on `stream`
+ * that was launched WITHOUT programmatic stream serialization.  A chain of
+ * dependent launches that each trigger at their start (this library's fused
+ * kernels and nie_linear do) can run several kernels back at once, so "not
+ * written by the kernel just before" is not enough: the metadata must predate
+ * the whole chain.  The engine writes it in its packing kernel and launches
+ * the q/k/v projection as a plain library GEMM between the two, which ends
+ * any chain; q and the new cache rows come from the RoPE + KV write right
+ * before.  Same arguments, results and errors as nie_paged_decode.
  */
 int nie_paged_decode_overlapped(const void* q, int64_t q_row_stride, void* out,
                                 int64_t out_row_stride, const void* key_cache,
@@ -230,13 +235,17 @@ int nie_paged_decode_overlapped(const void* q, int64_t q_row_stride, void* out,
  *    (about 840 requests at 32 query heads on a 148-SM B200); larger calls
  *    fail with NIE_ERR_INVALID and a message naming the limit.
  *  - The first call on a device looks up the array's device address with that
- *    device current; make that first call before any stream capture.
+ *    device current; make that first call before any stream capture.  An empty
+ *    batch (num_requests == 0) only checks its arguments and resolves nothing.
+ *  - Devices: ordinals 0 .. NIE_DECODE_NOALLOC_MAX_DEVICES-1 (64 GPUs per
+ *    process); a stream on a higher ordinal fails with NIE_ERR_INVALID.
  *  - Every call shares the one array, which keeps the last call's contents
  *    (the kernels need no zeroed scratch).  Calls that overlap on the GPU
  *    (several streams or host threads at once) race on it: serialize them.
  *  - Nothing is allocated: no cudaMalloc, cudaFree or allocating library call.
  */
 #define NIE_DECODE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+#define NIE_DECODE_NOALLOC_MAX_DEVICES 64
 
 /* Size in bytes of the fixed scratch array (NIE_DECODE_NOALLOC_SCRATCH_BYTES). */
 size_t nie_paged_decode_noalloc_capacity(void);
@@ -257,9 +266,9 @@ int nie_paged_decode_noalloc(const void* q, int64_t q_row_stride, void* out,
  * (d) Varlen causal attention over the paged cache (chunked prefill, and the
  * prefill rows of a mixed step).  Replaces the per-request write/gather/
  * attention loop of GroupedQueryAttention.forward_ragged
- * (nano_infer_engine/layers/attention.py:554-590) and the dense paged
+ * (nano_infer_engine/layers/attention.py:378-413) and the dense paged
  * prefill (nano_infer_engine/models/llama.py:274-325 with
- * attention.py:451-519).  The new keys/values must already be written into
+ * attention.py:275-343).  The new keys/values must already be written into
  * the cache (nie_write_kv).  For request r = req_list[i] (or i), its query
  * tokens are rows [query_start_loc[r], query_start_loc[r+1]) of q/out; the
  * token at offset j has position seq_lens[r] - qlen + j and attends to cached
@@ -308,7 +317,7 @@ int nie_add_rmsnorm(const void* x, const void* residual, const void* weight,
  * head_dim/2], activation dtype) with the half-split pairing, rotated q to
  * q_out [T, q_heads, head_dim], rotated k and v stored into the cache slots
  * (as nie_write_kv).  Replaces the RoPE of layers/rope.py:6-23 applied in
- * layers/attention.py:551-552 plus the slot write of paged_cache.py:324-382.
+ * layers/attention.py:375-376 plus the slot write of paged_cache.py:264-322.
  */
 int nie_rope_write_kv(const void* q, int64_t q_stride, const void* k,
                       int64_t k_stride, const void* v, int64_t v_stride,
@@ -380,6 +389,20 @@ int nie_linear(const void* x, int64_t ldx, const void* w, int64_t n, int64_t k,
 int nie_linear_overlapped(const void* x, int64_t ldx, const void* w, int64_t n,
                           int64_t k, int64_t m, void* y, int64_t ldy,
                           int32_t dtype, int32_t* err_flag, void* stream);
+
+/*
+ * nie_linear_timeout_test: failure-path test hook (no reference counterpart).
+ * Launches nie_linear's kernel with its producer issuing no copy, so every
+ * consumer's bounded mbarrier wait runs out after `wait_probes` probes
+ * (1 .. 2^22).  With no copy in flight, the kernel raises NIE_DEV_ERR_TIMEOUT
+ * in `err_flag`, joins its cluster barrier, writes zeros to y and returns;
+ * the context stays usable.  Checks that a timed-out wait ends the kernel
+ * instead of hanging it; never used on the data path.
+ */
+int nie_linear_timeout_test(const void* x, int64_t ldx, const void* w, int64_t n,
+                            int64_t k, int64_t m, void* y, int64_t ldy,
+                            int32_t dtype, int32_t* err_flag, void* stream,
+                            uint32_t wait_probes);
 
 #ifdef __cplusplus
 }

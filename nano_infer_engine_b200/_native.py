@@ -99,6 +99,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int32, c_void_p, c_void_p],
     ),
+    "nie_linear_timeout_test": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int32, c_void_p, c_void_p]
+        + [ctypes.c_uint32],
+    ),
     "nie_varlen_workspace_size": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "nie_varlen_attention": (
         c_int,

@@ -17,7 +17,7 @@ def _is_int(value: object) -> bool:
 
 
 class BlockAllocator:
-    """LIFO allocator of physical KV block ids (reference block_allocator.py:4)."""
+    """LIFO allocator of physical KV block ids (reference block_allocator.py:4-60)."""
 
     def __init__(self, num_blocks: int) -> None:
         if not _is_int(num_blocks):

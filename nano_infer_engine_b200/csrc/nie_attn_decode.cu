@@ -700,12 +700,15 @@ static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[NIE_DECO
 
 namespace {
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {nullptr};
+constexpr int kNoallocMaxDevices = NIE_DECODE_NOALLOC_MAX_DEVICES;
+void* g_noalloc_ptr[kNoallocMaxDevices] = {nullptr};
 
 // Resolve the device address of the scratch array on `device`, which must be
 // the current device.  Runs once per device (the first call on that device).
 int noalloc_scratch(int device, void** out) {
-  if (device < 0 || device >= 64) return nie::fail(NIE_ERR_INVALID, "device %d out of range", device);
+  if (device < 0 || device >= kNoallocMaxDevices)
+    return nie::fail(NIE_ERR_INVALID, "nie_paged_decode_noalloc: device ordinal %d outside 0..%d", device,
+                     kNoallocMaxDevices - 1);
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (g_noalloc_ptr[device] == nullptr) {
     void* p = nullptr;
@@ -730,18 +733,20 @@ extern "C" int nie_paged_decode_noalloc(const void* q, int64_t q_row_stride, voi
                                         const int64_t* q_rows, const int32_t* req_list, int32_t num_requests,
                                         float scale, int32_t* err_flag, void* stream) {
   NIE_REQUIRE(num_requests >= 0 && q_heads > 0, "num_requests must be non-negative and q_heads positive");
+  if (num_requests == 0)  // argument checks only: an empty batch never touches (or resolves) the scratch
+    return nie_paged_decode(q, q_row_stride, out, out_row_stride, key_cache, value_cache, dtype, layer, num_layers,
+                            num_blocks, block_size, kv_heads, head_dim, q_heads, block_tables, table_stride,
+                            table_rows, seq_lens, q_rows, req_list, 0, scale, nullptr, 0, err_flag, stream);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int dev = stream_device(s);
   const int sms = sm_count(dev);
   NIE_REQUIRE(sms > 0, "cannot query the SM count of device %d", dev);
-  if (num_requests > 0) {
-    const size_t need = ws_bytes(sms * kDecCtasPerSm, num_requests, q_heads);
-    if (need > (size_t)NIE_DECODE_NOALLOC_SCRATCH_BYTES)
-      return fail(NIE_ERR_INVALID,
-                  "nie_paged_decode_noalloc: %d requests x %d query heads need %zu bytes of scratch, above the "
-                  "fixed %d-byte array; use nie_paged_decode with a caller-provided workspace",
-                  num_requests, q_heads, need, NIE_DECODE_NOALLOC_SCRATCH_BYTES);
-  }
+  const size_t need = ws_bytes(sms * kDecCtasPerSm, num_requests, q_heads);
+  if (need > (size_t)NIE_DECODE_NOALLOC_SCRATCH_BYTES)
+    return fail(NIE_ERR_INVALID,
+                "nie_paged_decode_noalloc: %d requests x %d query heads need %zu bytes of scratch, above the "
+                "fixed %d-byte array; use nie_paged_decode with a caller-provided workspace",
+                num_requests, q_heads, need, NIE_DECODE_NOALLOC_SCRATCH_BYTES);
   int prev = -1;
   if (cudaGetDevice(&prev) != cudaSuccess) return fail(NIE_ERR_CUDA, "cudaGetDevice failed");
   if (prev != dev && cudaSetDevice(dev) != cudaSuccess) return fail(NIE_ERR_CUDA, "cudaSetDevice(%d) failed", dev);

@@ -6,7 +6,7 @@
 //   p   = round(exp(s - max) / sum exp(s - max))       (fp32 softmax, cast)
 //   out = round(sum p * v)                             (fp32-accumulated matmul)
 // following nano_infer_engine/layers/paged_attention.py:95-114 and
-// nano_infer_engine/layers/attention.py:576-587.  Two passes over the keys
+// nano_infer_engine/layers/attention.py:400-411.  Two passes over the keys
 // (max/sum, then the weighted sum) make the cast of normalised p exact.
 #include "nie_attn.cuh"
 

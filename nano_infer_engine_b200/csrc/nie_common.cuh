@@ -45,6 +45,10 @@ int opt_in_smem(int slot, const void* kernel, size_t bytes);
 // writes it must call pdl_wait(), which returns once the previous grid has
 // completed and its memory operations are visible.  Without the launch
 // attribute both instructions are no-ops.
+// Chains: when consecutive kernels all trigger at their start, a kernel may
+// begin while kernels SEVERAL launches back are still running, so anything
+// read before pdl_wait() must be complete before the most recent launch made
+// without the attribute (which ends every chain).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

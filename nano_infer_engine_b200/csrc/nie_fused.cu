@@ -8,7 +8,7 @@
 //                  (reference layers/rms_norm.py:25-31 and the residual adds of
 //                  layers/decoder.py:55-74)
 //   rope_write_kv: q' = rope(q); k' = rope(k); cache[slot] = k', v
-//                  (reference layers/rope.py:6-23 + paged_cache.py:324-382;
+//                  (reference layers/rope.py:6-23 + paged_cache.py:264-322;
 //                  the RoPE fusion into the slot write of the build plan)
 //   silu_mul     : out = silu(gate) * up  (reference layers/mlp.py:18-22)
 #include "nie_common.cuh"

@@ -64,6 +64,8 @@ struct LinearArgs {
   int ksteps;  // k-steps per n-tile (K / 64)
   int32_t* err;
   int early_weights;  // issue the first ring of weight loads before waiting for the previous kernel
+  uint32_t wait_probes;  // bound of every mbarrier wait (kLnWaitProbes outside the timeout test hook)
+  int withhold;          // timeout test hook: the producer issues no copy, so every consumer wait runs out
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -84,6 +86,17 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile(
       "barrier.cluster.arrive.release.aligned;\n\t"
       "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Split cluster barrier: every thread arrives once its CTA has started (after
+// the mbarrier set-up) and waits before its first remote shared-memory store,
+// so no CTA writes into a peer that has not started yet.  The wait sits after
+// the streaming loop, where all peers have long arrived.
+__device__ __forceinline__ void cluster_arrive_started() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_started() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
 // Store two floats at `local_addr` (an address in this CTA's shared window)
@@ -146,6 +159,7 @@ __global__ void __launch_bounds__(kLnThreads, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  cluster_arrive_started();
 
   if (warp == kLnConsumerWarps) {
     // ---------------- producer: one lane keeps the ring full
@@ -159,7 +173,10 @@ __global__ void __launch_bounds__(kLnThreads, 1)
       // the caller guarantees that kernel does not write w: the first ring of
       // weight tiles is already streaming while it finishes.
       int k = 0;
-      if (a.early_weights) {
+      if (a.withhold) {
+        pdl_wait();
+        k = steps;  // nothing issued: nothing in flight, no drain below
+      } else if (a.early_weights) {
         for (; k < steps && k < kLnStages; ++k) {
           mbar_arrive_expect_tx(&full[k], Lay::kStageBytes);
           tma_load_2d_hint(dsm + k * Lay::kStageBytes, &wmap, &full[k], (s0 + k) * kLnK, tile * ROWS, stream_once);
@@ -172,7 +189,7 @@ __global__ void __launch_bounds__(kLnThreads, 1)
       }
       for (; k < steps; ++k) {
         const int st = k % kLnStages;
-        if (k >= kLnStages && !mbar_wait_bounded(&empty[st], (uint32_t)((k / kLnStages) - 1) & 1u, kLnWaitProbes)) {
+        if (k >= kLnStages && !mbar_wait_bounded(&empty[st], (uint32_t)((k / kLnStages) - 1) & 1u, a.wait_probes)) {
           raise_flag(a.err, NIE_DEV_ERR_TIMEOUT);
           break;
         }
@@ -184,10 +201,12 @@ __global__ void __launch_bounds__(kLnThreads, 1)
       }
       // Copies of the last issued stages may still be landing if a consumer
       // gave up early: wait (bounded) for them before the CTA moves on.
-      for (int j = k > kLnStages ? k - kLnStages : 0; j < k; ++j)
-        mbar_wait_bounded(&full[j % kLnStages], (uint32_t)(j / kLnStages) & 1u, kLnWaitProbes);
+      if (!a.withhold)
+        for (int j = k > kLnStages ? k - kLnStages : 0; j < k; ++j)
+          mbar_wait_bounded(&full[j % kLnStages], (uint32_t)(j / kLnStages) & 1u, a.wait_probes);
     }
     __syncwarp();
+    cluster_wait_started();
   } else {
     // ---------------- consumers: warp w owns weight rows [w*ROWS/4, (w+1)*ROWS/4) of the tile
     const int g = lane >> 2, t = lane & 3;
@@ -197,7 +216,7 @@ __global__ void __launch_bounds__(kLnThreads, 1)
     for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
     for (int k = 0; k < steps; ++k) {
       const int st = k % kLnStages;
-      if (!mbar_wait_bounded(&full[st], (uint32_t)(k / kLnStages) & 1u, kLnWaitProbes)) {
+      if (!mbar_wait_bounded(&full[st], (uint32_t)(k / kLnStages) & 1u, a.wait_probes)) {
         if (lane == 0) raise_flag(a.err, NIE_DEV_ERR_TIMEOUT);
         break;
       }
@@ -225,7 +244,9 @@ __global__ void __launch_bounds__(kLnThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
-    // send each output pair's partial to the cluster CTA that owns it
+    // send each output pair's partial to the cluster CTA that owns it (every
+    // cluster CTA has started: see cluster_wait_started)
+    cluster_wait_started();
     const uint32_t rbase = smem_u32(recv);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -324,7 +345,8 @@ int opt_in_both(int dev) {
 using namespace nie;
 
 static int linear_impl(const void* x, int64_t ldx, const void* w, int64_t n, int64_t k, int64_t m, void* y,
-                       int64_t ldy, int32_t dtype, int32_t* err_flag, void* stream, bool early_weights) {
+                       int64_t ldy, int32_t dtype, int32_t* err_flag, void* stream, bool early_weights,
+                       bool withhold = false, uint32_t wait_probes = kLnWaitProbes) {
   NIE_REQUIRE(x && w && y, "null pointer argument");
   NIE_REQUIRE(m >= 0 && n > 0 && k > 0, "bad shape m=%lld n=%lld k=%lld", (long long)m, (long long)n, (long long)k);
   if (dtype != NIE_DTYPE_BF16 || m > kLnXRows || n % 64 != 0 || k % kLnK != 0 ||
@@ -395,6 +417,8 @@ static int linear_impl(const void* x, int64_t ldx, const void* w, int64_t n, int
   la.ksteps = ksteps;
   la.err = err_flag;
   la.early_weights = early_weights ? 1 : 0;
+  la.wait_probes = wait_probes;
+  la.withhold = withhold ? 1 : 0;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(tiles * cs));
   cfg.blockDim = dim3(kLnThreads);
@@ -423,4 +447,11 @@ extern "C" int nie_linear(const void* x, int64_t ldx, const void* w, int64_t n, 
 extern "C" int nie_linear_overlapped(const void* x, int64_t ldx, const void* w, int64_t n, int64_t k, int64_t m,
                                      void* y, int64_t ldy, int32_t dtype, int32_t* err_flag, void* stream) {
   return linear_impl(x, ldx, w, n, k, m, y, ldy, dtype, err_flag, stream, true);
+}
+
+extern "C" int nie_linear_timeout_test(const void* x, int64_t ldx, const void* w, int64_t n, int64_t k, int64_t m,
+                                       void* y, int64_t ldy, int32_t dtype, int32_t* err_flag, void* stream,
+                                       uint32_t wait_probes) {
+  NIE_REQUIRE(wait_probes > 0 && wait_probes <= kLnWaitProbes, "wait_probes must be in [1, %u]", kLnWaitProbes);
+  return linear_impl(x, ldx, w, n, k, m, y, ldy, dtype, err_flag, stream, false, true, wait_probes);
 }

@@ -1,4 +1,4 @@
-"""Generation settings (reference generation/config.py:6-50)."""
+"""Generation settings (reference generation/config.py:7-50)."""
 
 from __future__ import annotations
 

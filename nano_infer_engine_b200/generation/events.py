@@ -1,4 +1,4 @@
-"""Scheduler outputs (reference generation/events.py:8-33)."""
+"""Scheduler outputs (reference generation/events.py:9-33)."""
 
 from __future__ import annotations
 

@@ -1,4 +1,4 @@
-"""Offline greedy driver over the scheduler (reference generation/paged_greedy.py:11-91)."""
+"""Offline greedy driver over the scheduler (reference generation/paged_greedy.py:12-91)."""
 
 from __future__ import annotations
 

@@ -43,7 +43,7 @@ def pd_greedy_generate(
     decode_cache: PagedKVCache,
     sequence_id: str = "default",
 ) -> GenerationOutput:
-    """Prefill, hand the KV over, then decode one request (reference pd_greedy.py:30-137)."""
+    """Prefill, hand the KV over, then decode one request (reference pd_greedy.py:31-137)."""
     if not config.use_cache:
         raise ValueError("P/D generation requires config.use_cache=True")
     if input_ids.ndim != 2 or input_ids.shape[0] != 1:

@@ -174,7 +174,7 @@ class ContinuousBatchingScheduler:
             self.paged_cache.release(sequence_id)
 
     def _admit_pending_requests(self) -> list[PagedRequest]:
-        """Non-chunked admission with one batched prefill (reference scheduler.py:196-253)."""
+        """Non-chunked admission with one batched prefill (reference scheduler.py:190-253)."""
         if self.config.prefill_chunk_size is not None:
             self._admit_chunked_requests()
             return []
@@ -417,7 +417,7 @@ class ContinuousBatchingScheduler:
 
     @torch.inference_mode()
     def step(self) -> SchedulerStepOutput:
-        """One iteration (reference scheduler.py:485-578)."""
+        """One iteration (reference scheduler.py:486-578)."""
         if self._closed:
             raise RuntimeError("scheduler is closed")
         if self.config.prefill_chunk_size is not None:

@@ -1,4 +1,4 @@
-"""Pre-norm Llama decoder block (reference layers/decoder.py:6-74)."""
+"""Pre-norm Llama decoder block (reference layers/decoder.py:7-74)."""
 
 from __future__ import annotations
 

@@ -1,4 +1,4 @@
-"""SwiGLU feed-forward block (reference layers/mlp.py:5-22); dense GEMMs stay on torch."""
+"""SwiGLU feed-forward block (reference layers/mlp.py:7-22); dense GEMMs stay on torch."""
 
 from __future__ import annotations
 

@@ -52,7 +52,7 @@ class RopeScalingConfig:
 
 @dataclass
 class LlamaConfig:
-    """Same fields and defaults as reference models/llama.py:22-70."""
+    """Same fields and defaults as reference models/llama.py:23-70."""
 
     vocab_size: int = 128256
     hidden_size: int = 2048

@@ -3,7 +3,7 @@
 Every function here requires CUDA tensors and calls the sm_100a library; there
 is no CPU implementation.  Shapes follow the reference's cache layout
 ``[num_layers, num_blocks, block_size, kv_heads, head_dim]``
-(nano_infer_engine/paged_cache.py:131-139).
+(nano_infer_engine/paged_cache.py:71-79).
 """
 
 from __future__ import annotations
@@ -612,6 +612,12 @@ def linear_eligible(x: torch.Tensor, weight: torch.Tensor) -> bool:
     cluster beats the library GEMM (B200, CUDA graphs, 16 rows: o_proj 4.6 vs
     5.5 us, down_proj 9.6 vs 12.9 us); for K < N (q/k/v, gate/up) the library
     GEMM is faster.
+
+    Routing q/k/v here as well would make every kernel between the packing
+    kernel and the attention a dependent launch; the overlapped decode reads
+    its metadata before waiting and relies on the plain cuBLAS q/k/v launch to
+    end that chain (see ``nie_paged_decode_overlapped`` in the C header): such
+    a change must move the decode's metadata reads after its wait.
     """
     return (
         STREAM_LINEAR

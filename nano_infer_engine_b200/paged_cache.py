@@ -7,15 +7,15 @@ what changes is where the data moves:
 * every sequence also owns a row of a device-resident int32 block-table
   array (``[rows, stride]``), updated incrementally when blocks are
   allocated, so kernels resolve slots on the GPU instead of per token in
-  Python (reference paged_cache.py:300-322);
+  Python (reference paged_cache.py:306-322);
 * ``write`` / ``gather`` / ``export_sequence`` / ``import_sequence`` run the
   slot-write, gather and block-copy kernels (one launch each) instead of
   per-token / per-block ``copy_`` loops;
 * :func:`transfer_sequence` copies a sequence straight from one pool's
   blocks into freshly allocated blocks of another pool (NVLink peer copy
   when the pools are on different GPUs), the P/D handoff of
-  nano_infer_engine/generation/pd_scheduler.py:253-262 without the
-  intermediate stacked tensor.
+  nano_infer_engine/generation/pd_scheduler.py:144-145 (export_sequence
+  then import_sequence) without the intermediate stacked tensor.
 """
 
 from __future__ import annotations
@@ -41,7 +41,7 @@ def _check_sequence_id(sequence_id: object) -> None:
 
 @dataclass(frozen=True)
 class PagedKVTransfer:
-    """Logical blocks exported from one cache (reference paged_cache.py:8-19)."""
+    """Logical blocks exported from one cache (reference paged_cache.py:9-19)."""
 
     sequence_id: str
     sequence_length: int
@@ -54,7 +54,7 @@ class PagedKVTransfer:
 
 
 class PagedKVCache:
-    """Physical K/V blocks plus per-sequence block tables (reference paged_cache.py:22)."""
+    """Physical K/V blocks plus per-sequence block tables (reference paged_cache.py:22-374)."""
 
     _INITIAL_ROWS = 16
     _INITIAL_COLS = 64

@@ -1,7 +1,7 @@
 """Torch-CPU restatement of the reference's paged attention (test oracle).
 
 Rounding sequence of the reference (layers/paged_attention.py:95-114 and
-layers/attention.py:571-588): scores are a ``dtype`` matmul output, scaled in
+layers/attention.py:395-411): scores are a ``dtype`` matmul output, scaled in
 ``dtype``; softmax runs in fp32; probabilities are cast to ``dtype``; the PV
 product is a ``dtype`` matmul.  Inputs are CPU tensors.
 """
@@ -12,7 +12,7 @@ import torch
 
 
 def gather_sequence(cache: torch.Tensor, layer: int, table: list[int], length: int) -> torch.Tensor:
-    """paged_cache.py:384-422: logical-order rows [length, H, D] of one sequence."""
+    """paged_cache.py:324-362: logical-order rows [length, H, D] of one sequence."""
     bs = cache.shape[2]
     blocks = torch.tensor(table[: (length + bs - 1) // bs], dtype=torch.long)
     rows = cache[layer, blocks].reshape(-1, cache.shape[3], cache.shape[4])
@@ -56,7 +56,7 @@ def varlen_attention(
     query_lengths: list[int],
     layer: int,
 ) -> torch.Tensor:
-    """attention.py:554-588 after the write: query [T, Hq, D] -> [T, Hq, D], causal per request."""
+    """attention.py:392-413 after the write: query [T, Hq, D] -> [T, Hq, D], causal per request."""
     group = query.shape[1] // key_cache.shape[3]
     outs = []
     start = 0

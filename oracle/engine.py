@@ -5,7 +5,7 @@ Follows (paths relative to the reference's src/nano_infer_engine/):
   layers/rms_norm.py:25-31             fp32 RMSNorm
   layers/mlp.py:18-22                  SwiGLU
   layers/decoder.py:55-74              pre-norm residual block (ragged)
-  layers/attention.py:521-590          ragged attention: write, gather, causal softmax
+  layers/attention.py:345-414          ragged attention: write, gather, causal softmax
   models/llama.py:339-394              forward_ragged: capacity, layers, lm_head, advance
 It is the checker and the timed CPU baseline, never part of the product.
 """
@@ -22,7 +22,7 @@ from .paging import OracleTables
 
 def inv_freq(dim: int, theta: float, rope_type: str = "default", scaling: dict | None = None) -> torch.Tensor:
     i = torch.arange(0, dim, 2, dtype=torch.float32)
-    base = 1 / theta ** (i / dim)  # rope.py:28-29
+    base = 1 / theta ** (i / dim)  # rope.py:33-35 (and :108)
     if rope_type == "default":
         return base
     s = scaling or {}
@@ -30,7 +30,7 @@ def inv_freq(dim: int, theta: float, rope_type: str = "default", scaling: dict |
     low_f = s.get("low_freq_factor", 1.0)
     high_f = s.get("high_freq_factor", 4.0)
     orig = s.get("original_max_position_embeddings", 8192)
-    wavelen = 2 * math.pi / base  # rope.py:106-141
+    wavelen = 2 * math.pi / base  # rope.py:110-145
     scaled = base / factor
     smooth = (orig / wavelen - low_f) / (high_f - low_f)
     smooth_freq = (1 - smooth) * scaled + smooth * base
@@ -42,7 +42,7 @@ def inv_freq(dim: int, theta: float, rope_type: str = "default", scaling: dict |
 
 
 def rope(x: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
-    """x [T, H, D]; rope.py:184-194 (position_ids branch) then :6-23."""
+    """x [T, H, D]; rope.py:184-198 (position_ids branch) then :6-23."""
     angles = positions.to(torch.float32)[:, None] * freqs
     sin = torch.sin(angles).to(x.dtype)[:, None, :]
     cos = torch.cos(angles).to(x.dtype)[:, None, :]
@@ -67,7 +67,7 @@ class OracleCache:
         self.block_size = block_size
 
     def write(self, layer: int, sid: str, start: int, k: torch.Tensor, v: torch.Tensor) -> None:
-        """paged_cache.py:324-382 restated with index arithmetic instead of a token loop."""
+        """paged_cache.py:264-322 restated with index arithmetic instead of a token loop."""
         slots = torch.tensor([self.tables.slot(sid, start + j) for j in range(k.shape[0])], dtype=torch.long)
         bs = self.block_size
         self.keys[layer, slots // bs, slots % bs] = k

@@ -67,8 +67,8 @@ class OracleTables:
 def ragged_metadata(
     tables: list[list[int]], contexts: list[int], query_lengths: list[int], block_size: int
 ) -> dict[str, list[int]]:
-    """query_start_loc (paged_prefill.py:132-143), positions (attention.py:539-550),
-    slot mapping (paged_cache.py:313-322 via :240-262), last rows (paged_prefill.py:154)."""
+    """query_start_loc (paged_prefill.py:132-143), positions (attention.py:363-376),
+    slot mapping (paged_cache.py:311-322 via :240-262), last rows (paged_prefill.py:154)."""
     qsl = [0]
     for q in query_lengths:
         qsl.append(qsl[-1] + q)

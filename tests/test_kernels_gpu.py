@@ -123,7 +123,7 @@ def test_gather_kv_bit_exact(cuda):
 # ------------------------------------------------------------------ (e)
 @pytest.mark.parametrize("length", [16, 37, 1])
 def test_copy_blocks_export_semantics(cuda, length):
-    """Block copy with a zeroed tail == reference export_sequence (paged_cache.py:205-240)."""
+    """Block copy with a zeroed tail == reference export_sequence (paged_cache.py:145-180)."""
     g = torch.Generator().manual_seed(length)
     L, nb, bs = 3, 20, 16
     kc = torch.randn(L, nb, bs, 8, 64, generator=g).to(torch.bfloat16)
@@ -544,3 +544,37 @@ def test_overlapped_linear_after_the_kernel_that_writes_x(cuda, n, k):
     ops().check_device_errors(cuda)
     assert torch.equal(outs[0], outs[1])
     torch.testing.assert_close(outs[0].float(), act.float() @ w.float().T, atol=2e-3, rtol=2 ** -7)
+
+
+def test_bounded_wait_times_out_and_the_kernel_returns(cuda):
+    """Failure path of the bounded mbarrier waits, without a fault: the timeout hook launches
+    nie_linear's kernel with nothing issued on its copy ring, so every consumer wait runs out.
+    The kernel must return (the call completes), raise NIE_DEV_ERR_TIMEOUT, leave zeros, and the
+    next normal launch on the same context must be clean and correct."""
+    from nano_infer_engine_b200 import _native
+
+    lib = _native.lib
+    g = torch.Generator().manual_seed(5)
+    m, n, k = 16, 2048, 8192  # K split over a cluster: the timed-out CTAs still meet at its barrier
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(cuda)
+    w = (torch.randn(n, k, generator=g) / k ** 0.5).to(torch.bfloat16).to(cuda)
+    y = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    rc = lib.nie_linear_timeout_test(x.data_ptr(), k, w.data_ptr(), n, k, m, y.data_ptr(), n, _native.NIE_DTYPE_BF16,
+                                     err.data_ptr(), stream, 1000)
+    assert rc == 0, lib.nie_last_error()
+    torch.cuda.synchronize(cuda)
+    assert int(err.item()) & _native.NIE_DEV_ERR_TIMEOUT
+    assert torch.equal(y, torch.zeros_like(y))
+    # the context is still usable: a normal launch is clean and right
+    err.zero_()
+    rc = lib.nie_linear(x.data_ptr(), k, w.data_ptr(), n, k, m, y.data_ptr(), n, _native.NIE_DTYPE_BF16,
+                        err.data_ptr(), stream)
+    assert rc == 0, lib.nie_last_error()
+    torch.cuda.synchronize(cuda)
+    assert int(err.item()) == 0
+    torch.testing.assert_close(y.float(), x.float() @ w.float().T, atol=1e-3, rtol=2 ** -7)
+    # probe counts outside [1, 2^22] are refused on the host
+    assert lib.nie_linear_timeout_test(x.data_ptr(), k, w.data_ptr(), n, k, m, y.data_ptr(), n,
+                                       _native.NIE_DTYPE_BF16, err.data_ptr(), stream, 0) == _native.NIE_ERR_INVALID

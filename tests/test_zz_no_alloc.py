@@ -23,6 +23,7 @@ def _inputs(seed, batch, max_ctx, device):
     g = torch.Generator().manual_seed(seed)
     bs = 16
     lens = torch.randint(1, max_ctx + 1, (batch,), generator=g).tolist()
+    lens[0] = max_ctx  # at least one request as long as asked
     blocks = sum(-(-n // bs) for n in lens)
     nb = blocks + 9
     perm = torch.randperm(nb, generator=g)
@@ -66,7 +67,9 @@ def test_noalloc_decode_matches_the_allocating_entry_point_on_consecutive_calls(
         torch.cuda.synchronize(cuda)
         assert int(err.item()) == 0
         assert torch.isfinite(got).all()
-        torch.testing.assert_close(got.float(), want.float(), atol=2e-2, rtol=0)
+        # same kernels, same inputs: only the scratch location differs, so the
+        # results are bitwise equal
+        assert torch.equal(got, want)
 
 
 def test_noalloc_decode_rejects_batches_beyond_its_scratch(cuda):
@@ -82,3 +85,51 @@ def test_noalloc_decode_rejects_batches_beyond_its_scratch(cuda):
     rc = lib.nie_paged_decode_noalloc(*args, None, torch.cuda.current_stream(cuda).cuda_stream)
     assert rc == _native.NIE_ERR_INVALID
     assert b"scratch" in lib.nie_last_error()
+
+
+def test_noalloc_decode_edge_of_its_scratch(cuda):
+    """The largest batch that fits the fixed array runs (and matches the allocating
+    entry point); one request more is rejected before any launch."""
+    lib = _native.lib
+    dev = cuda.index or 0
+    cap = lib.nie_paged_decode_noalloc_capacity()
+    fits = 1
+    while lib.nie_paged_decode_workspace_size(dev, fits + 1, 32, 64) <= cap:
+        fits += 1
+    assert lib.nie_paged_decode_workspace_size(dev, fits, 32, 64) <= cap
+    assert lib.nie_paged_decode_workspace_size(dev, fits + 1, 32, 64) > cap
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    q, kc, vc, tables, lens = _inputs(3, fits + 1, 40, cuda)
+    # the largest batch that fits: the first `fits` requests of the inputs
+    sub = (q[:fits], kc, vc, tables[:fits], lens[:fits])
+    want = torch.empty_like(sub[0])
+    ws_bytes = lib.nie_paged_decode_workspace_size(dev, fits, 32, 64)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda)
+    rc = lib.nie_paged_decode(*_common_args(sub[0], want, *sub[1:]), ws.data_ptr(), ws_bytes, err.data_ptr(), stream)
+    assert rc == 0, lib.nie_last_error()
+    got = torch.full_like(want, float("nan"))
+    rc = lib.nie_paged_decode_noalloc(*_common_args(sub[0], got, *sub[1:]), err.data_ptr(), stream)
+    assert rc == 0, lib.nie_last_error()
+    torch.cuda.synchronize(cuda)
+    assert int(err.item()) == 0
+    assert torch.equal(got, want)
+    # one more request: rejected, nothing launched, output untouched
+    out = torch.full_like(q, float("nan"))
+    rc = lib.nie_paged_decode_noalloc(*_common_args(q, out, kc, vc, tables, lens), err.data_ptr(), stream)
+    assert rc == _native.NIE_ERR_INVALID
+    assert b"scratch" in lib.nie_last_error()
+    torch.cuda.synchronize(cuda)
+    assert torch.isnan(out.float()).all()
+
+
+def test_noalloc_decode_empty_batch_is_a_no_op(cuda):
+    lib = _native.lib
+    q, kc, vc, tables, lens = _inputs(4, 2, 20, cuda)
+    out = torch.full_like(q, float("nan"))
+    args = _common_args(q, out, kc, vc, tables, lens)
+    args[20] = 0  # num_requests
+    rc = lib.nie_paged_decode_noalloc(*args, None, torch.cuda.current_stream(cuda).cuda_stream)
+    assert rc == 0, lib.nie_last_error()
+    torch.cuda.synchronize(cuda)
+    assert torch.isnan(out.float()).all()
