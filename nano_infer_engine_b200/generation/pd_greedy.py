@@ -1,36 +1,55 @@
-"""Synchronous single-request prefill/decode disaggregation (reference generation/pd_greedy.py).
+"""Synchronous prefill/decode disaggregation of one request (the reference's
+generation/pd_greedy.py API).
 
-The KV handoff is :func:`transfer_sequence`: one block-copy kernel from the
-prefill pool straight into the decode pool (NVLink peer stores when the
-pools are on different GPUs), instead of export -> stacked tensor -> per
-block cross-device ``copy_`` (reference pd_greedy.py:86-87).
+The request is handed over with :class:`PDPair` (one ragged prefill, a
+block-to-block KV copy into the decode pool, prefill blocks freed), then
+decoded greedily on the decode engine.  Generated ids go into a preallocated
+device row and each next input is a view of it: no growing ``torch.cat`` per
+token, and no device-to-host read per token unless an EOS id is configured
+(only then must each token be inspected before the next forward).
 """
 
 from __future__ import annotations
 
 import torch
 
-from ..paged_cache import PagedKVCache, transfer_sequence
+from ..paged_cache import PagedKVCache
 from .config import GenerationConfig, GenerationOutput
-from .paged_prefill import _validate_paged_prefill_inputs, paged_prefill
+from .pd_handoff import PDPair, blocks_for, drop
 
 
-def _validate_model_cache(model, cache: PagedKVCache, name: str) -> None:
-    if model.embed.weight.device != cache.keys.device:
-        raise ValueError(f"{name} model and cache must be on the same device")
-    if model.embed.weight.dtype != cache.keys.dtype:
-        raise ValueError(f"{name} model and cache must have the same dtype")
-    if len(model.decoders) != cache.num_layers:
-        raise ValueError(f"{name} model and cache must have the same layer count")
-    if model.config.kv_head_num != cache.kv_head_num:
-        raise ValueError(f"{name} model and cache must have the same KV head count")
-    if model.config.head_dim != cache.head_dim:
-        raise ValueError(f"{name} model and cache must have the same head dimension")
+def _check_call(input_ids: torch.Tensor, config: GenerationConfig) -> None:
+    if not config.use_cache:
+        raise ValueError("P/D generation requires config.use_cache=True")
+    if input_ids.ndim != 2 or input_ids.shape[0] != 1:
+        raise ValueError("input_ids must have shape (1, prompt_length)")
+    if input_ids.shape[1] <= 0:
+        raise ValueError("input_ids must contain at least one token")
 
 
-def _release_if_allocated(cache: PagedKVCache, sequence_id: str) -> None:
-    if sequence_id in cache._block_tables:
-        cache.release(sequence_id)
+def _greedy_decode(decode_model, cache: PagedKVCache, sequence_id: str, prompt: torch.Tensor,
+                   first_logits: torch.Tensor, config: GenerationConfig) -> GenerationOutput:
+    dev = cache.keys.device
+    start = prompt.shape[1]
+    row = torch.empty((1, start + config.max_new_tokens), dtype=prompt.dtype, device=dev)
+    row[:, :start].copy_(prompt)
+    eos = config.eos_token_id
+    logits = first_logits.reshape(1, -1)
+    produced, hit_eos = 0, False
+    while produced < config.max_new_tokens:
+        at = start + produced
+        row[:, at : at + 1] = logits.argmax(dim=-1, keepdim=True)
+        produced += 1
+        if eos is not None and int(row[0, at]) == eos:
+            hit_eos = True
+            break
+        if produced < config.max_new_tokens:
+            logits = decode_model(row[:, at : at + 1], kv_cache=cache, sequence_id=sequence_id)[:, -1]
+    return GenerationOutput(
+        sequences=row[:, : start + produced],
+        generated_tokens=torch.full((1,), produced, dtype=torch.long, device=dev),
+        stopped_by_eos=torch.full((1,), hit_eos, dtype=torch.bool, device=dev),
+    )
 
 
 @torch.inference_mode()
@@ -43,56 +62,22 @@ def pd_greedy_generate(
     decode_cache: PagedKVCache,
     sequence_id: str = "default",
 ) -> GenerationOutput:
-    """Prefill, hand the KV over, then decode one request (reference pd_greedy.py:31-137)."""
-    if not config.use_cache:
-        raise ValueError("P/D generation requires config.use_cache=True")
-    if input_ids.ndim != 2 or input_ids.shape[0] != 1:
-        raise ValueError("input_ids must have shape (1, prompt_length)")
-    if input_ids.shape[1] <= 0:
-        raise ValueError("input_ids must contain at least one token")
-    if not isinstance(prefill_cache, PagedKVCache):
-        raise TypeError("prefill_cache must be a PagedKVCache")
-    if not isinstance(decode_cache, PagedKVCache):
-        raise TypeError("decode_cache must be a PagedKVCache")
-    if prefill_cache is decode_cache:
-        raise ValueError("prefill_cache and decode_cache must be different caches")
-    _validate_model_cache(prefill_model, prefill_cache, "prefill")
-    _validate_model_cache(decode_model, decode_cache, "decode")
-    _validate_paged_prefill_inputs((input_ids,), prefill_cache, (sequence_id,))
-    if sequence_id in decode_cache._block_tables:
-        raise ValueError(f"sequence ID already exists: {sequence_id}")
-    capacity = input_ids.shape[1] + config.max_new_tokens - 1
-    bs = decode_cache.block_size
-    if (capacity + bs - 1) // bs > decode_cache.allocator.free_block_count:
+    """Prefill on the prefill engine, hand the KV over, decode greedily on the decode engine.
+
+    The prefill pool ends with no blocks of the request.  On success the decode
+    pool keeps the sequence (the caller may inspect, continue or release it);
+    on any failure it keeps nothing of it.
+    """
+    _check_call(input_ids, config)
+    pair = PDPair.checked(prefill_model, decode_model, prefill_cache, decode_cache)
+    pair.check_new(sequence_id, input_ids)
+    worst_case = blocks_for(input_ids.shape[1] + config.max_new_tokens - 1, decode_cache.block_size)
+    if worst_case > decode_cache.allocator.free_block_count:
         raise ValueError("not enough free blocks in decode cache")
-
-    device = decode_cache.keys.device
+    (first_logits,) = pair.hand_off([sequence_id], [input_ids])
     try:
-        last_logits = paged_prefill(prefill_model, (input_ids,), prefill_cache, (sequence_id,))
-        transfer_sequence(prefill_cache, decode_cache, sequence_id)
-        last_logits = last_logits.to(device)
+        return _greedy_decode(decode_model, decode_cache, sequence_id, input_ids.to(pair.decode_device),
+                              first_logits, config)
     except Exception:
-        _release_if_allocated(decode_cache, sequence_id)
+        drop(decode_cache, sequence_id)
         raise
-    finally:
-        _release_if_allocated(prefill_cache, sequence_id)
-
-    sequences = input_ids.to(device)
-    generated = torch.zeros(1, dtype=torch.long, device=device)
-    stopped = torch.zeros(1, dtype=torch.bool, device=device)
-    try:
-        for step in range(config.max_new_tokens):
-            next_token = last_logits.argmax(dim=-1, keepdim=True)
-            sequences = torch.cat((sequences, next_token), dim=1)
-            generated += 1
-            if config.eos_token_id is not None:
-                stopped |= next_token.squeeze(-1).eq(config.eos_token_id)
-                if stopped.all():
-                    break
-            if step + 1 < config.max_new_tokens:
-                logits = decode_model(next_token, kv_cache=decode_cache, sequence_id=sequence_id)
-                last_logits = logits[:, -1]
-    except Exception:
-        _release_if_allocated(decode_cache, sequence_id)
-        raise
-    return GenerationOutput(sequences=sequences, generated_tokens=generated, stopped_by_eos=stopped)

@@ -5,9 +5,12 @@ to its `src` directory (the one holding the `nano_infer_engine` package):
 
     NIE_REFERENCE_SRC=<reference>/src python tests/golden/make_golden.py
 
-It imports the reference package ``nano_infer_engine`` and this repository's
-seeded recipes (tests/golden/recipes.py) and writes only reference OUTPUTS:
-paging.json, decode_<case>.pt, ragged_<case>.pt, config1_tokens.json.
+It imports the reference package ``nano_infer_engine``, this repository's
+seeded recipes (tests/golden/recipes.py) and the oracle's seeded weight
+recipe (oracle/weights.py; nothing from the product package), and writes only
+reference OUTPUTS: paging.json, decode_<case>.pt, ragged_<case>.pt,
+config1_tokens.json, pd_tokens.json (``--pd``) and config2_tokens.json
+(``--config2``).
 """
 
 from __future__ import annotations
@@ -35,7 +38,14 @@ from nano_infer_engine.layers.rope import Rope  # noqa: E402
 from nano_infer_engine.models.llama import Llama3_2, LlamaConfig  # noqa: E402
 from nano_infer_engine.paged_cache import PagedKVCache  # noqa: E402
 
-from nano_infer_engine_b200.models.llama import init_random_weights_  # noqa: E402
+from oracle.weights import LLAMA_1B, random_llama_state  # noqa: E402
+
+
+def _reference_llama(kwargs: dict, seed: int, std: float, dtype: torch.dtype, **extra) -> Llama3_2:
+    """The reference's Llama3_2 holding the seeded random-init weights."""
+    model = Llama3_2(LlamaConfig(**kwargs, **extra)).to(dtype).eval()
+    model.load_state_dict(random_llama_state(kwargs, seed, std, dtype))
+    return model
 
 
 def paging() -> dict:
@@ -102,9 +112,8 @@ def ragged(name: str) -> dict:
 
 
 def config1() -> dict:
-    torch.manual_seed(0)
-    model = Llama3_2(LlamaConfig(**recipes.config1_kwargs())).eval()
-    init_random_weights_(model, recipes.CONFIG1_WEIGHT_SEED, recipes.CONFIG1_STD)
+    model = _reference_llama(recipes.config1_kwargs(), recipes.CONFIG1_WEIGHT_SEED, recipes.CONFIG1_STD,
+                             torch.float32)
     cache = PagedKVCache(64, 16, 2, 2, 64, torch.float32, "cpu")
     config = GenerationConfig(max_new_tokens=16, prefill_chunk_size=32)
     sched = ContinuousBatchingScheduler(model, config, cache, 4)
@@ -139,12 +148,7 @@ def config1() -> dict:
 def config2_reduced() -> dict:
     """BASELINE config 2 (Llama-3.2-1B shape, bf16, random init std 0.02) with the
     bench's seeded workload but only CONFIG2_NEW_TOKENS new tokens per request."""
-    from nano_infer_engine_b200.models.llama import LlamaConfig as OurConfig, build_random_llama
-
-    ours = build_random_llama(OurConfig(max_seq_len=29600), recipes.CONFIG2_WEIGHT_SEED, 0.02, torch.bfloat16, "cpu")
-    model = Llama3_2(LlamaConfig(max_seq_len=29600)).to(torch.bfloat16).eval()
-    model.load_state_dict(ours.state_dict())
-    del ours
+    model = _reference_llama(LLAMA_1B, recipes.CONFIG2_WEIGHT_SEED, 0.02, torch.bfloat16, max_seq_len=29600)
     prompts = recipes.config2_prompts()
     blocks = sum((p.shape[1] + recipes.CONFIG2_NEW_TOKENS + 15) // 16 for p in prompts) + 16
     cache = PagedKVCache(blocks, 16, 16, 8, 64, torch.bfloat16, "cpu")
@@ -168,7 +172,103 @@ def config2_reduced() -> dict:
     }
 
 
+def pd_pipeline() -> dict:
+    """The reference's PDContinuousBatchingScheduler and pd_greedy_generate on the
+    config-1 model (fp32, both caches on the host): every step's token events and
+    terminal requests, the decode pool's block table of each request at hand-off,
+    both pools' occupancy after each step, and the greedy margins."""
+    from nano_infer_engine.generation.pd_greedy import pd_greedy_generate
+    from nano_infer_engine.generation.pd_scheduler import PDContinuousBatchingScheduler
+
+    kwargs = recipes.config1_kwargs()
+
+    def model():
+        return _reference_llama(kwargs, recipes.CONFIG1_WEIGHT_SEED, recipes.CONFIG1_STD, torch.float32)
+
+    def cache(blocks):
+        return PagedKVCache(blocks, 16, 2, 2, 64, torch.float32, "cpu")
+
+    config = GenerationConfig(max_new_tokens=recipes.PD_NEW_TOKENS, eos_token_id=None)
+    sched = PDContinuousBatchingScheduler(model(), model(), config, cache(recipes.PD_PREFILL_BLOCKS),
+                                          cache(recipes.PD_DECODE_BLOCKS), recipes.PD_MAX_BATCH)
+    prompts = recipes.pd_prompts()
+    ids = [f"pd-{i}" for i in range(len(prompts))]
+    reqs = [sched.add_request(s, p) for s, p in zip(ids, prompts)]
+    handoff_tables: dict[str, list[int]] = {}
+    admit = sched.decode_scheduler.add_prefilled_request
+
+    def recording_admit(request, last_logits):
+        handoff_tables[request.sequence_id] = list(sched.decode_cache.get_block_table(request.sequence_id))
+        return admit(request, last_logits)
+
+    sched.decode_scheduler.add_prefilled_request = recording_admit
+    margins: dict[str, list[float]] = {s: [] for s in ids}
+    decode_step = sched.decode_scheduler.step
+
+    def recording_step():
+        for r in sched.decode_scheduler.active_requests:
+            top2 = r.last_logits.float().topk(2).values
+            margins[r.sequence_id].append(float(top2[0] - top2[1]))
+        return decode_step()
+
+    sched.decode_scheduler.step = recording_step
+    steps = []
+    with torch.inference_mode():
+        while sched.has_work:
+            out = sched.step()
+            steps.append({
+                "events": [[e.sequence_id, e.token_id] for e in out.token_events],
+                "terminal": [[r.sequence_id, r.status.name] for r in out.terminal_requests],
+                "pending": sched.pending_count,
+                "active": sched.active_count,
+                "decode_free": sched.decode_cache.allocator.free_block_count,
+                "prefill_allocated": sched.prefill_cache.allocator.allocated_block_count,
+            })
+    scheduler_out = {
+        "tokens": {r.sequence_id: r.sequence[0, r.prompt.shape[1]:].tolist() for r in reqs},
+        "status": {r.sequence_id: r.status.name for r in reqs},
+        "handoff_tables": handoff_tables,
+        "steps": steps,
+        "margins": margins,
+    }
+
+    # pd_greedy_generate: two requests in a row through the same caches (the
+    # decode pool keeps each finished sequence), then one stopped by EOS
+    greedy = []
+    prefill_model, decode_model = model(), model()
+    prefill_cache, decode_cache = cache(recipes.PD_GREEDY_BLOCKS), cache(recipes.PD_GREEDY_BLOCKS)
+    gprompts = recipes.pd_prompts(recipes.PD_GREEDY_PROMPT_LENS, seed=22)
+    gconfig = GenerationConfig(max_new_tokens=recipes.PD_GREEDY_NEW_TOKENS, eos_token_id=None)
+    for i, p in enumerate(gprompts):
+        out = pd_greedy_generate(prefill_model, decode_model, p, gconfig, prefill_cache, decode_cache, f"g-{i}")
+        greedy.append({
+            "sequence": out.sequences[0].tolist(),
+            "generated": out.generated_tokens.tolist(),
+            "stopped_by_eos": out.stopped_by_eos.tolist(),
+            "decode_table": list(decode_cache.get_block_table(f"g-{i}")),
+            "decode_length": decode_cache.get_sequence_length(f"g-{i}"),
+            "prefill_allocated": prefill_cache.allocator.allocated_block_count,
+        })
+    eos = greedy[0]["sequence"][gprompts[0].shape[1] + recipes.PD_GREEDY_EOS_INDEX]
+    econfig = GenerationConfig(max_new_tokens=recipes.PD_GREEDY_NEW_TOKENS, eos_token_id=eos)
+    prefill_cache, decode_cache = cache(recipes.PD_GREEDY_BLOCKS), cache(recipes.PD_GREEDY_BLOCKS)
+    out = pd_greedy_generate(prefill_model, decode_model, gprompts[0], econfig, prefill_cache, decode_cache, "g-eos")
+    eos_out = {
+        "eos_token_id": eos,
+        "sequence": out.sequences[0].tolist(),
+        "generated": out.generated_tokens.tolist(),
+        "stopped_by_eos": out.stopped_by_eos.tolist(),
+        "decode_table": list(decode_cache.get_block_table("g-eos")),
+        "decode_length": decode_cache.get_sequence_length("g-eos"),
+    }
+    return {"scheduler": scheduler_out, "greedy": greedy, "greedy_eos": eos_out}
+
+
 def main() -> None:
+    if "--pd" in sys.argv:
+        (HERE / "pd_tokens.json").write_text(json.dumps(pd_pipeline()))
+        print("pd golden written")
+        return
     if "--config2" in sys.argv:
         (HERE / "config2_tokens.json").write_text(json.dumps(config2_reduced()))
         print("config2 golden written")

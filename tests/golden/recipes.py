@@ -114,3 +114,24 @@ def config2_prompts(num_requests: int = 16, seed: int = 1234) -> list[torch.Tens
     g = torch.Generator().manual_seed(seed)
     lengths = torch.randint(128, 2049, (num_requests,), generator=g).tolist()
     return [torch.randint(0, 128256, (1, n), generator=g) for n in lengths]
+
+
+# ------------------------------------------------------------ P/D pipeline
+# BASELINE config-1 model (fp32) behind the prefill/decode pipeline: six
+# prompts, 16 new tokens, a decode pool small enough that the worst-case
+# block reservation (not only the batch slots) holds requests back.
+PD_PROMPT_LENS = (7, 33, 64, 100, 1, 45)
+PD_NEW_TOKENS = 16
+PD_MAX_BATCH = 3
+PD_PREFILL_BLOCKS = 32
+PD_DECODE_BLOCKS = 12
+# pd_greedy_generate: two requests through shared caches, then one with EOS
+PD_GREEDY_PROMPT_LENS = (33, 100)
+PD_GREEDY_NEW_TOKENS = 12
+PD_GREEDY_BLOCKS = 16
+PD_GREEDY_EOS_INDEX = 4  # EOS = the token the first request generated at this index
+
+
+def pd_prompts(lengths=PD_PROMPT_LENS, seed: int = 21) -> list[torch.Tensor]:
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randint(0, 1024, (1, n), generator=g) for n in lengths]

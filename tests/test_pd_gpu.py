@@ -1,30 +1,36 @@
-"""P/D disaggregation on two GPUs.
+"""P/D disaggregation across processes (and across GPUs where the box has two).
 
 * ``transfer_sequence`` inside one process, cuda:0 -> cuda:1 (the block-copy
-  kernel writing into the peer's pool over NVLink);
-* a prefill process on cuda:0 and a decode process on cuda:1: the decode
-  process maps the prefill pool with CUDA IPC and pulls each request's blocks
-  with the same kernel.  The KV bytes on both sides must be identical and
-  the greedy tokens must equal a single-GPU run of the same model (fp32, so
-  that batching differences cannot flip a token).  Two passes over the same
-  requests reuse the channel, both pools and the sequence ids.
-
-Both tests skip on a box with fewer than two GPUs.
+  kernel writing into the peer's pool over NVLink); skipped on one GPU;
+* a prefill process and a decode process (on cuda:0 and cuda:1, or both on
+  cuda:0 when the box has one GPU): the decode process maps the prefill
+  process's pool with CUDA IPC and pulls each request's blocks with the same
+  kernel.  No kernel of one process waits on the other (the channel is on the
+  host), so sharing one GPU is safe.  The KV bytes on both sides must be
+  identical, and the greedy tokens must equal the reference's own P/D
+  scheduler run on the same model and prompts (tests/golden/pd_tokens.json,
+  config-1 model in fp32).  Two passes over the same requests reuse the
+  channel, both pools and the sequence ids.
 """
 
+import json
 import socket
 from datetime import timedelta
+from pathlib import Path
 
 import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+import recipes
+
 pytestmark = pytest.mark.gpu
 
-PROMPT_LENS = (5, 40, 77, 16, 130, 300, 1, 64)
-NEW_TOKENS = 12
+NEW_TOKENS = recipes.PD_NEW_TOKENS
 PASSES = 2
+PREFILL_BLOCKS = 12  # holds a few prompts at a time: later batches wait for ACKs
+GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "pd_tokens.json").read_text())
 
 
 def _need_two_gpus():
@@ -32,17 +38,20 @@ def _need_two_gpus():
         pytest.skip("needs two CUDA devices")
 
 
+def _devices():
+    """(prefill device, decode device): two GPUs when present, else both on cuda:0."""
+    return (0, 1) if torch.cuda.device_count() >= 2 else (0, 0)
+
+
 def _model(device):
     from nano_infer_engine_b200.models.llama import LlamaConfig, build_random_llama
 
-    cfg = LlamaConfig(vocab_size=512, hidden_size=512, mlp_inner_size=1024, num_layers=2, q_head_num=8,
-                      kv_head_num=2, max_seq_len=4096)
-    return build_random_llama(cfg, 11, 0.02, torch.float32, device), cfg
+    cfg = LlamaConfig(**recipes.config1_kwargs())
+    return build_random_llama(cfg, recipes.CONFIG1_WEIGHT_SEED, recipes.CONFIG1_STD, torch.float32, device), cfg
 
 
 def _prompts(cfg):
-    g = torch.Generator().manual_seed(5)
-    return [torch.randint(0, cfg.vocab_size, (1, n), generator=g) for n in PROMPT_LENS]
+    return recipes.pd_prompts()
 
 
 def test_transfer_sequence_between_devices_is_bit_exact():
@@ -77,7 +86,7 @@ def test_transfer_sequence_between_devices_is_bit_exact():
     assert not dst.keys[:, last, n % 16 :].any() and not dst.values[:, last, n % 16 :].any()
 
 
-def _pair_worker(rank, port, out):
+def _pair_worker(rank, port, out, devices):
     from nano_infer_engine_b200 import ops
     from nano_infer_engine_b200.generation.config import GenerationConfig
     from nano_infer_engine_b200.generation.pd_disagg import (
@@ -93,8 +102,8 @@ def _pair_worker(rank, port, out):
     )
     from nano_infer_engine_b200.paged_cache import PagedKVCache
 
-    torch.cuda.set_device(rank)
-    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(devices[rank])
+    dev = torch.device("cuda", devices[rank])
     store = dist.TCPStore("127.0.0.1", port, 2, rank == 0, timeout=timedelta(seconds=120))
     model, cfg = _model(dev)
     prompts = [p.to(dev) for p in _prompts(cfg)]
@@ -106,8 +115,7 @@ def _pair_worker(rank, port, out):
         saved[sid] = [tuple(t.cpu() for t in cache.gather(li, sid, n)) for li in range(layers)]
 
     if rank == 0:
-        # 40 blocks hold a few prompts at a time: later batches wait for ACKs
-        cache = PagedKVCache(40, 16, layers, cfg.kv_head_num, cfg.head_dim, torch.float32, dev)
+        cache = PagedKVCache(PREFILL_BLOCKS, 16, layers, cfg.kv_head_num, cfg.head_dim, torch.float32, dev)
         publish_pool(store, 0, cache)
         release = cache.release
 
@@ -118,7 +126,7 @@ def _pair_worker(rank, port, out):
         cache.release = release_and_record
         with torch.inference_mode():
             for _ in range(PASSES):  # passes reuse the channel, both pools and the sequence ids
-                stats = run_prefill(model, cache, channel, list(enumerate(prompts)), token_budget=256,
+                stats = run_prefill(model, cache, channel, list(enumerate(prompts)), token_budget=96,
                                     idle_sleep=0.0005)
         ops.check_device_errors(dev)
         wait_pool_unmapped(store, 1)
@@ -155,29 +163,21 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_prefill_decode_pair_processes_match_single_gpu(tmp_path):
-    _need_two_gpus()
-    from nano_infer_engine_b200.generation.config import GenerationConfig
-    from nano_infer_engine_b200.generation.scheduler import ContinuousBatchingScheduler
-    from nano_infer_engine_b200.paged_cache import PagedKVCache
-
+def test_prefill_decode_pair_processes_match_reference_golden(tmp_path):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    devices = _devices()
     path = str(tmp_path / "pair")
-    mp.start_processes(_pair_worker, args=(_free_port(), path), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_pair_worker, args=(_free_port(), path, devices), nprocs=2, start_method="spawn", join=True)
     pre = torch.load(path + ".0")
     dec = torch.load(path + ".1")
     assert pre["batches"] > 1
-    assert pre["free"] == 40 and dec["free"] == 256
-    assert sorted(pre["kv"]) == sorted(dec["kv"]) == sorted(f"pd-{i}" for i in range(len(PROMPT_LENS)))
+    assert pre["free"] == PREFILL_BLOCKS and dec["free"] == 256
+    ids = [f"pd-{i}" for i in range(len(recipes.PD_PROMPT_LENS))]
+    assert sorted(pre["kv"]) == sorted(dec["kv"]) == sorted(ids)
     for sid, layers in pre["kv"].items():
         for (kp, vp), (kd, vd) in zip(layers, dec["kv"][sid]):
             assert torch.equal(kp, kd) and torch.equal(vp, vd), sid
-
-    dev = torch.device("cuda", 0)
-    model, cfg = _model(dev)
-    cache = PagedKVCache(256, 16, cfg.num_layers, cfg.kv_head_num, cfg.head_dim, torch.float32, dev)
-    sched = ContinuousBatchingScheduler(model, GenerationConfig(max_new_tokens=NEW_TOKENS), cache, 4)
-    reqs = [sched.add_request(f"pd-{i}", p.to(dev)) for i, p in enumerate(_prompts(cfg))]
-    with torch.inference_mode():
-        sched.run_until_idle()
-    want = {r.sequence_id: r.sequence[0].tolist() for r in reqs}
+    prompts = recipes.pd_prompts()
+    want = {sid: p[0].tolist() + GOLDEN["scheduler"]["tokens"][sid] for sid, p in zip(ids, prompts)}
     assert dec["tokens"] == want
