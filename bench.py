@@ -470,10 +470,9 @@ def run_pd_open(args, dist_ctx, rank, local, device, world):
 
 
 # ------------------------------------------------------ decode roofline
-def decode_config3(device, iters, B=64, nb=131072):
-    """BASELINE config 3: B=64, ctx U[512, 29600], pool 131072 blocks, 1 layer."""
-    from nano_infer_engine_b200 import ops
-
+def config3_inputs(device, B=64, nb=131072):
+    """BASELINE config 3 inputs (seeded): B requests, ctx U[512, 29600], block tables
+    consecutive slices of a random permutation of an nb-block pool, 1 layer, N(0, 1)."""
     g = torch.Generator().manual_seed(0)
     bs = 16
     lens = torch.randint(512, 29601, (B,), generator=g).tolist()
@@ -491,8 +490,17 @@ def decode_config3(device, iters, B=64, nb=131072):
     kc = torch.randn((1, nb, bs, 8, 64), generator=gen, device=device, dtype=torch.bfloat16)
     vc = torch.randn((1, nb, bs, 8, 64), generator=gen, device=device, dtype=torch.bfloat16)
     q = torch.randn((B, 32, 64), generator=gen, device=device, dtype=torch.bfloat16)
-    tables_d = tables.to(device)
-    lens_d = torch.tensor(lens, dtype=torch.int32, device=device)
+    return {"q": q, "kc": kc, "vc": vc, "tables": tables, "lens": lens, "tables_d": tables.to(device),
+            "lens_d": torch.tensor(lens, dtype=torch.int32, device=device)}
+
+
+def decode_config3(device, iters, B=64, nb=131072):
+    """BASELINE config 3: B=64, ctx U[512, 29600], pool 131072 blocks, 1 layer."""
+    from nano_infer_engine_b200 import ops
+
+    bs = 16
+    inp = config3_inputs(device, B, nb)
+    q, kc, vc, tables_d, lens_d, lens = inp["q"], inp["kc"], inp["vc"], inp["tables_d"], inp["lens_d"], inp["lens"]
     out = torch.empty_like(q)
     for _ in range(3):
         ops.paged_decode(q, kc, vc, 0, tables_d, lens_d, out=out)
@@ -512,11 +520,10 @@ def decode_config3(device, iters, B=64, nb=131072):
     return {"ms": ms, "bytes": algo_bytes, "sum_ctx": sum_ctx, "batch": B}
 
 
-def mixed_config4(device, iters):
-    """BASELINE config 4: 8 prefill chunks of 128 at ctx U[0, 8192] + 120 decode rows at
-    ctx U[256, 16384] (prefill first), one layer of the Llama-1B attention shape.
-    Times the tcgen05 varlen kernels (attention + split-KV combine) and the
-    decode kernels separately, each as `iters` calls replayed from a CUDA graph."""
+def config4_inputs(device):
+    """BASELINE config 4 inputs (seeded): 8 prefill chunks of 128 at ctx U[0, 8192] then
+    120 decode rows at ctx U[256, 16384], random block tables, 1 layer, N(0, 1); the
+    ragged metadata comes from the packing kernel."""
     from nano_infer_engine_b200 import ops
 
     g = torch.Generator().manual_seed(4)
@@ -541,16 +548,46 @@ def mixed_config4(device, iters):
     R = len(lens)
     plan = torch.tensor([list(range(R)), contexts, qlens], dtype=torch.int32).to(device)
     meta = ops.pack_ragged(plan, T, tables.to(device), bs, nb, num_decode=120, max_query_len=128)
-    out = torch.empty_like(q)
+    return {"q": q, "kc": kc, "vc": vc, "tables": tables, "contexts": contexts, "qlens": qlens, "lens": lens,
+            "meta": meta}
+
+
+def config4_prefill(inp, out):
+    """The prefill rows of the config-4 step on the tcgen05 kernel (split-KV workspace)."""
+    from nano_infer_engine_b200 import ops
+
+    m = inp["meta"]
+    ops.varlen_attention(inp["q"], inp["kc"], inp["vc"], 0, m.block_tables, m.seq_lens, m.query_start_loc, 128,
+                         out=out, table_rows=m.table_rows, req_list=m.prefill_list, num_requests=8,
+                         max_seq_len=max(inp["lens"][:8]))
+
+
+def config4_decode(inp, out):
+    """The decode rows of the config-4 step on the split-K decode kernel."""
+    from nano_infer_engine_b200 import ops
+
+    m = inp["meta"]
+    ops.paged_decode(inp["q"], inp["kc"], inp["vc"], 0, m.block_tables, m.seq_lens, out=out,
+                     table_rows=m.table_rows, q_rows=m.query_start_loc, req_list=m.decode_list, num_requests=120)
+
+
+def mixed_config4(device, iters):
+    """BASELINE config 4: 8 prefill chunks of 128 at ctx U[0, 8192] + 120 decode rows at
+    ctx U[256, 16384] (prefill first), one layer of the Llama-1B attention shape.
+    Times the tcgen05 varlen kernels (attention + split-KV combine) and the
+    decode kernels separately, each as `iters` calls replayed from a CUDA graph."""
+    from nano_infer_engine_b200 import ops
+
+    bs = 16
+    inp = config4_inputs(device)
+    contexts, lens = inp["contexts"], inp["lens"]
+    out = torch.empty_like(inp["q"])
 
     def prefill():
-        ops.varlen_attention(q, kc, vc, 0, meta.block_tables, meta.seq_lens, meta.query_start_loc, 128, out=out,
-                             table_rows=meta.table_rows, req_list=meta.prefill_list, num_requests=8,
-                             max_seq_len=max(lens[:8]))
+        config4_prefill(inp, out)
 
     def decode():
-        ops.paged_decode(q, kc, vc, 0, meta.block_tables, meta.seq_lens, out=out, table_rows=meta.table_rows,
-                         q_rows=meta.query_start_loc, req_list=meta.decode_list, num_requests=120)
+        config4_decode(inp, out)
 
     res = {}
     for name, fn in (("prefill", prefill), ("decode", decode)):
@@ -574,11 +611,12 @@ def mixed_config4(device, iters):
         del graph
     ops.check_device_errors(device)
     flops = sum(4 * 64 * 32 * (128 * c + 128 * 129 // 2) for c in contexts[:8])
+    kc, vc = inp["kc"], inp["vc"]
     dec_bytes = sum(lens[8:]) * 2048 + sum(-(-n // bs) for n in lens[8:]) * 4 + 2 * 120 * 32 * 64 * 2
     res.update(prefill_flops=flops, prefill_tflops=flops / (res["prefill_ms"] / 1e3) / 1e12,
                decode_bytes=dec_bytes, decode_gbs=dec_bytes / (res["decode_ms"] / 1e3) / 1e9,
                prefill_contexts=contexts[:8])
-    del kc, vc
+    del kc, vc, inp
     torch.cuda.empty_cache()
     return res
 
@@ -639,6 +677,54 @@ def measured_peaks():
         data = json.loads(path.read_text())
         return float(data["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def measured_tensor_peaks():
+    """(burst, sustained) dense bf16 TFLOP/s and their source."""
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["bf16_tflops"]), float(data.get("bf16_tflops_sustained", data["bf16_tflops"])), "measured"
+    return 1590.0, 1400.0, "fallback"
+
+
+# Llama-3.2-1B: parameters streamed per decode step (embedding table read once, as the
+# tied lm_head) and the per-token matmul parameters of the 16 decoder layers
+LLAMA_1B_PARAMS = 128256 * 2048 + 16 * (2 * 2048 * 2048 + 2 * 512 * 2048 + 3 * 8192 * 2048)
+LLAMA_1B_LAYER_PARAMS = 16 * (2 * 2048 * 2048 + 2 * 512 * 2048 + 3 * 8192 * 2048)
+KV_BYTES_PER_TOKEN = 16 * 2 * 8 * 64 * 2  # all layers, K and V, bf16
+
+
+def workload_roofline(prompt_lens, new_tokens, ms_per_generation):
+    """Ideal time of one config-2 generation on this GPU and the measured fraction of it.
+
+    Decode (HBM-bound): the first token of each request comes from its prefill;
+    each of the other new_tokens - 1 forwards streams every weight once per step
+    (batched over the requests) and reads the request's cached KV (context
+    prompt + s at step s).  Prefill (tensor-bound): 2 x layer parameters per
+    prompt token, plus causal attention 4 x 64 x 32 x L(L+1)/2 per layer, plus
+    one lm_head row per request.  Ideal = bytes / HBM peak + FLOPs / sustained
+    bf16 peak (the step runs for seconds under the power cap).
+    """
+    hbm, _ = measured_peaks()
+    _, sustained, kind = measured_tensor_peaks()
+    steps = new_tokens - 1
+    decode_bytes = steps * LLAMA_1B_PARAMS * 2 + sum(
+        sum(L + s for s in range(1, new_tokens)) for L in prompt_lens) * KV_BYTES_PER_TOKEN
+    prefill_flops = sum(2 * LLAMA_1B_LAYER_PARAMS * L + 16 * 4 * 64 * 32 * L * (L + 1) // 2
+                        + 2 * 128256 * 2048 for L in prompt_lens)
+    ideal_s = decode_bytes / (hbm * 1e9) + prefill_flops / (sustained * 1e12)
+    return {
+        "bound": "hbm (decode steps) + tensor (prefill)",
+        "ideal_ms": ideal_s * 1e3,
+        "measured_ms": ms_per_generation,
+        "frac": ideal_s * 1e3 / ms_per_generation,
+        "decode_bytes": decode_bytes,
+        "prefill_flops": prefill_flops,
+        "peaks": {"hbm_gbs": hbm, "bf16_tflops_sustained": sustained, "kind": kind},
+        "note": "ideal = algorithmic decode bytes / HBM peak + prefill FLOPs / sustained bf16 peak, "
+                "per generation of the batch; frac = ideal / measured",
+    }
 
 
 def ncu_traffic():
@@ -851,6 +937,17 @@ def main():
                 "workload": f"config3 decode: B=64, sum ctx {dec['sum_ctx']}, {dec['bytes']} algorithmic bytes/launch",
                 "ms_per_launch": dec["ms"], "peak_kind": f"{peak_kind} (hbm_gbs burst copy)"}
 
+    mixed = mixed_config4(device, args.decode_iters)
+    burst, _, tkind = measured_tensor_peaks()
+    roofline_prefill = {"bound": "tensor", "achieved": mixed["prefill_tflops"], "peak": burst, "unit": "TFLOP/s",
+                        "frac": mixed["prefill_tflops"] / burst, "kernel": "prefill_tc_kernel + prefill_combine_kernel",
+                        "workload": f"config4 prefill rows: 8 x 128 queries at contexts {mixed['prefill_contexts']}, "
+                                    f"{mixed['prefill_flops']} causal FLOPs/call",
+                        "ms_per_launch": mixed["prefill_ms"], "peak_kind": f"{tkind} (bf16_tflops burst)",
+                        "decode_rows_gbs": mixed["decode_gbs"]}
+    roofline_workload = workload_roofline([p.shape[1] for p in host_prompts], args.new_tokens,
+                                          elapsed / args.steps * 1e3)
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         del model
@@ -873,6 +970,8 @@ def main():
             "data": "synthetic (seeded prompts, random-init weights N(0, 0.02))",
             "config": headline_config(args, world),
             "roofline": roofline,
+            "roofline_workload": roofline_workload,
+            "roofline_prefill": roofline_prefill,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,

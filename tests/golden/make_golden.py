@@ -9,8 +9,8 @@ It imports the reference package ``nano_infer_engine``, this repository's
 seeded recipes (tests/golden/recipes.py) and the oracle's seeded weight
 recipe (oracle/weights.py; nothing from the product package), and writes only
 reference OUTPUTS: paging.json, decode_<case>.pt, ragged_<case>.pt,
-config1_tokens.json, pd_tokens.json (``--pd``) and config2_tokens.json
-(``--config2``).
+config1_tokens.json, pd_tokens.json (``--pd``) and config2_greedy256.json
+(``--config2-dense``).
 """
 
 from __future__ import annotations
@@ -145,33 +145,6 @@ def config1() -> dict:
     }
 
 
-def config2_reduced() -> dict:
-    """BASELINE config 2 (Llama-3.2-1B shape, bf16, random init std 0.02) with the
-    bench's seeded workload but only CONFIG2_NEW_TOKENS new tokens per request."""
-    model = _reference_llama(LLAMA_1B, recipes.CONFIG2_WEIGHT_SEED, 0.02, torch.bfloat16, max_seq_len=29600)
-    prompts = recipes.config2_prompts()
-    blocks = sum((p.shape[1] + recipes.CONFIG2_NEW_TOKENS + 15) // 16 for p in prompts) + 16
-    cache = PagedKVCache(blocks, 16, 16, 8, 64, torch.bfloat16, "cpu")
-    config = GenerationConfig(max_new_tokens=recipes.CONFIG2_NEW_TOKENS, prefill_chunk_size=128,
-                              max_prefill_tokens_per_step=512)
-    sched = ContinuousBatchingScheduler(model, config, cache, len(prompts))
-    ids = [f"req-{i}" for i in range(len(prompts))]
-    reqs = [sched.add_request(s, p) for s, p in zip(ids, prompts)]
-    # margin (top-1 minus top-2 logit) of every greedy decision, read from the
-    # logits each active request holds right before the step that samples it
-    margins: dict[str, list[float]] = {s: [] for s in ids}
-    with torch.inference_mode():
-        while sched.has_work:
-            for r in sched.active_requests:
-                top2 = r.last_logits.float().topk(2).values
-                margins[r.sequence_id].append(float(top2[0] - top2[1]))
-            sched.step()
-    return {
-        "tokens": {r.sequence_id: r.sequence[0, r.prompt.shape[1]:].tolist() for r in reqs},
-        "margins": margins,
-    }
-
-
 def pd_pipeline() -> dict:
     """The reference's PDContinuousBatchingScheduler and pd_greedy_generate on the
     config-1 model (fp32, both caches on the host): every step's token events and
@@ -264,14 +237,46 @@ def pd_pipeline() -> dict:
     return {"scheduler": scheduler_out, "greedy": greedy, "greedy_eos": eos_out}
 
 
+def config2_dense() -> dict:
+    """BASELINE config 2 in full: the 16 seeded prompts, 256 greedy tokens each, bf16,
+    through the reference's dense greedy_generate (generation/greedy.py:10-122), one
+    request at a time (no padding), with the top-1 minus top-2 logit margin of every
+    greedy decision.  The reference pins this path equal to its paged scheduler
+    (tests/test_paged_greedy_generation.py:145-200); its paged path would take hours
+    here because of the per-token Python gather loops."""
+    from nano_infer_engine.generation.greedy import greedy_generate
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    model = _reference_llama(LLAMA_1B, recipes.CONFIG2_WEIGHT_SEED, 0.02, torch.bfloat16, max_seq_len=29600)
+    config = GenerationConfig(max_new_tokens=recipes.CONFIG2_FULL_NEW_TOKENS, eos_token_id=None)
+    forward = model.forward
+    margins: list[float] = []
+
+    def recording(*args, **kwargs):
+        logits = forward(*args, **kwargs)
+        top2 = logits[0, -1].float().topk(2).values
+        margins.append(float(top2[0] - top2[1]))
+        return logits
+
+    model.forward = recording
+    out_tokens, out_margins = {}, {}
+    for i, prompt in enumerate(recipes.config2_prompts()):
+        margins.clear()
+        out = greedy_generate(model, prompt, config)
+        out_tokens[f"req-{i}"] = out.sequences[0, prompt.shape[1]:].tolist()
+        out_margins[f"req-{i}"] = list(margins)
+        print(f"config2 dense: request {i} ({prompt.shape[1]} prompt tokens) done", flush=True)
+    return {"new_tokens": recipes.CONFIG2_FULL_NEW_TOKENS, "tokens": out_tokens, "margins": out_margins}
+
+
 def main() -> None:
+    if "--config2-dense" in sys.argv:
+        (HERE / "config2_greedy256.json").write_text(json.dumps(config2_dense()))
+        print("config2 dense golden written")
+        return
     if "--pd" in sys.argv:
         (HERE / "pd_tokens.json").write_text(json.dumps(pd_pipeline()))
         print("pd golden written")
-        return
-    if "--config2" in sys.argv:
-        (HERE / "config2_tokens.json").write_text(json.dumps(config2_reduced()))
-        print("config2 golden written")
         return
     (HERE / "paging.json").write_text(json.dumps(paging(), indent=1))
     for name in recipes.DECODE_CASES:

@@ -106,7 +106,7 @@ CONFIG1_STD = 0.02
 
 # BASELINE config 2 (Llama-3.2-1B shape, bf16): the bench's seeded workload
 CONFIG2_WEIGHT_SEED = 1234
-CONFIG2_NEW_TOKENS = 8
+CONFIG2_FULL_NEW_TOKENS = 256  # the full config-2 generation (dense reference golden)
 
 
 def config2_prompts(num_requests: int = 16, seed: int = 1234) -> list[torch.Tensor]:

@@ -1,0 +1,112 @@
+"""BASELINE config 2 greedy tokens against the reference, all 256 of them.
+
+Golden: ``tests/golden/make_golden.py --config2-dense`` ran the reference's
+own greedy_generate (bf16, Llama-3.2-1B shape, random init std 0.02) on the
+bench's 16 seeded prompts for 256 new tokens each, and stored every token
+with the reference's top-1 minus top-2 logit margin at that decision.
+
+bf16 greedy decoding of a random-init model has exact ties and near ties,
+and the CPU and the B200 accumulate in different orders, so a token can flip
+where the reference itself barely preferred it.  Two checks:
+
+* teacher-forced: each prompt + the reference's continuation goes through
+  this package's ``forward_ragged`` in one ragged step, so every one of the
+  4096 decisions is scored on the reference's own history.  The argmax must
+  equal the reference's token wherever the reference's margin exceeds
+  MARGIN_BOUND; every mismatch is reported with its margin, and the number
+  of matching decisions is pinned (at least MIN_TEACHER_FORCED_MATCHES);
+* free-running: the engine's own generation (the bench's scheduler path:
+  chunked prefill 128, at most 512 prefill tokens per step, CUDA-graph
+  decode) follows the reference token for token until its first difference,
+  which must fall on a reference decision with margin <= MARGIN_BOUND.
+"""
+
+import json
+from pathlib import Path
+
+import pytest
+import torch
+
+import recipes
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "config2_greedy256.json").read_text())
+# bf16 logits of this model are O(1): one ulp is 2^-7 .. 2^-6, so 0.0625 is 4-8 ulps
+MARGIN_BOUND = 0.0625
+MIN_TEACHER_FORCED_MATCHES = 4096 - 16  # measured on B200; a lower count means a numerics change
+
+
+def _model(cuda):
+    from nano_infer_engine_b200.models.llama import LlamaConfig, build_random_llama
+
+    return build_random_llama(LlamaConfig(max_seq_len=29600), recipes.CONFIG2_WEIGHT_SEED, 0.02, torch.bfloat16,
+                              cuda)
+
+
+def test_config2_teacher_forced_256_tokens_match_reference(cuda):
+    from nano_infer_engine_b200 import ops
+    from nano_infer_engine_b200.paged_cache import PagedKVCache
+
+    model = _model(cuda)
+    prompts = recipes.config2_prompts()
+    n_new = GOLDEN["new_tokens"]
+    longest = max(p.shape[1] for p in prompts) + n_new
+    cache = PagedKVCache(-(-longest // 16) + 4, 16, 16, 8, 64, torch.bfloat16, cuda)
+    matched, total, mismatches = 0, 0, []
+    with torch.inference_mode():
+        for i, prompt in enumerate(prompts):
+            sid = f"req-{i}"
+            ref = GOLDEN["tokens"][sid]
+            margins = GOLDEN["margins"][sid]
+            assert len(ref) == len(margins) == n_new
+            seq = torch.cat([prompt[0], torch.tensor(ref[:-1])]).to(cuda)
+            L = prompt.shape[1]
+            qsl = torch.tensor([0, seq.numel()], dtype=torch.long, device=cuda)
+            logits = model.forward_ragged(seq, kv_cache=cache, sequence_ids=(sid,), query_start_loc=qsl)
+            ours = ops.argmax_rows(logits[L - 1 : L - 1 + n_new]).tolist()
+            cache.release(sid)
+            for k, (a, b) in enumerate(zip(ours, ref)):
+                total += 1
+                if a == b:
+                    matched += 1
+                else:
+                    mismatches.append((sid, k, a, b, margins[k]))
+    ops.check_device_errors(cuda)
+    report = f"teacher-forced: {matched}/{total} decisions match; mismatches (id, pos, ours, ref, ref margin): " \
+             f"{mismatches}"
+    print(report)
+    assert total == 16 * n_new
+    assert all(m[4] <= MARGIN_BOUND for m in mismatches), report
+    assert matched >= MIN_TEACHER_FORCED_MATCHES, report
+
+
+def test_config2_free_running_generation_tracks_reference(cuda):
+    from nano_infer_engine_b200.generation.config import GenerationConfig
+    from nano_infer_engine_b200.generation.scheduler import ContinuousBatchingScheduler
+    from nano_infer_engine_b200.paged_cache import PagedKVCache
+
+    model = _model(cuda)
+    prompts = [p.to(cuda) for p in recipes.config2_prompts()]
+    n_new = GOLDEN["new_tokens"]
+    blocks = sum(-(-(p.shape[1] + n_new) // 16) for p in prompts) + 16
+    cache = PagedKVCache(blocks, 16, 16, 8, 64, torch.bfloat16, cuda)
+    config = GenerationConfig(max_new_tokens=n_new, prefill_chunk_size=128, max_prefill_tokens_per_step=512)
+    sched = ContinuousBatchingScheduler(model, config, cache, len(prompts))
+    reqs = [sched.add_request(f"req-{i}", p) for i, p in enumerate(prompts)]
+    with torch.inference_mode():
+        sched.run_until_idle()
+    agree, firsts = 0, []
+    for r in reqs:
+        ours = r.sequence[0, r.prompt.shape[1]:].tolist()
+        ref = GOLDEN["tokens"][r.sequence_id]
+        margins = GOLDEN["margins"][r.sequence_id]
+        assert len(ours) == len(ref) == n_new
+        k = next((k for k, (a, b) in enumerate(zip(ours, ref)) if a != b), n_new)
+        agree += k
+        if k < n_new:
+            firsts.append((r.sequence_id, k, margins[k]))
+    report = f"free-running: {agree}/{16 * n_new} tokens before each request's first difference; " \
+             f"first differences (id, pos, ref margin): {firsts}"
+    print(report)
+    assert all(m <= MARGIN_BOUND for _, _, m in firsts), report

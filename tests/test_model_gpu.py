@@ -96,49 +96,6 @@ def test_config1_greedy_tokens_and_step_plan_match_reference(cuda):
     assert cache.allocator.free_block_count == golden["free_blocks_after"]
 
 
-def test_config2_greedy_tokens_agree_with_reference_up_to_near_ties(cuda):
-    """BASELINE config 2 (Llama-3.2-1B shape, bf16, random init) against the reference run on CPU.
-
-    bf16 greedy decoding on a random-init model has exact and near ties, and
-    the CPU and B200 accumulate dot products in different orders, so tokens
-    are compared position by position up to each request's first difference;
-    that difference must fall on a decision the reference itself made with a
-    top-1/top-2 logit margin <= 0.125 (a few bf16 ulps of the logits).
-    """
-    from nano_infer_engine_b200.generation.config import GenerationConfig
-    from nano_infer_engine_b200.generation.scheduler import ContinuousBatchingScheduler
-    from nano_infer_engine_b200.models.llama import LlamaConfig, build_random_llama
-    from nano_infer_engine_b200.paged_cache import PagedKVCache
-
-    golden = json.loads((GOLDEN / "config2_tokens.json").read_text())
-    model = build_random_llama(LlamaConfig(max_seq_len=29600), recipes.CONFIG2_WEIGHT_SEED, 0.02, torch.bfloat16, cuda)
-    prompts = [p.to(cuda) for p in recipes.config2_prompts()]
-    blocks = sum((p.shape[1] + recipes.CONFIG2_NEW_TOKENS + 15) // 16 for p in prompts) + 16
-    cache = PagedKVCache(blocks, 16, 16, 8, 64, torch.bfloat16, cuda)
-    config = GenerationConfig(max_new_tokens=recipes.CONFIG2_NEW_TOKENS, prefill_chunk_size=128,
-                              max_prefill_tokens_per_step=512)
-    sched = ContinuousBatchingScheduler(model, config, cache, len(prompts))
-    reqs = [sched.add_request(f"req-{i}", p) for i, p in enumerate(prompts)]
-    with torch.inference_mode():
-        sched.run_until_idle()
-    matched = 0
-    total = 0
-    for r in reqs:
-        ours = r.sequence[0, r.prompt.shape[1]:].tolist()
-        ref = golden["tokens"][r.sequence_id]
-        margins = golden["margins"][r.sequence_id]
-        assert len(ours) == len(ref)
-        for k, (a, b) in enumerate(zip(ours, ref)):
-            total += 1
-            if a != b:
-                assert margins[k] <= 0.125, (r.sequence_id, k, a, b, margins[k])
-                total += len(ref) - k - 1
-                break
-            matched += 1
-    # the first token of every request follows prefill only; most must agree
-    assert matched >= 0.5 * total, (matched, total)
-
-
 def _llama_shaped_model(cuda, seed=7):
     """Llama attention geometry (head_dim 64, 4 q heads per kv head, bf16) at small width."""
     from nano_infer_engine_b200.models.llama import LlamaConfig, build_random_llama
