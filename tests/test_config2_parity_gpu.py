@@ -31,10 +31,15 @@ import recipes
 
 pytestmark = pytest.mark.gpu
 
-GOLDEN = json.loads((Path(__file__).resolve().parent / "golden" / "config2_greedy256.json").read_text())
+GOLDEN_PATH = Path(__file__).resolve().parent / "golden" / "config2_greedy256.json"
 # bf16 logits of this model are O(1): one ulp is 2^-7 .. 2^-6, so 0.0625 is 4-8 ulps
 MARGIN_BOUND = 0.0625
 MIN_TEACHER_FORCED_MATCHES = 4096 - 16  # measured on B200; a lower count means a numerics change
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return json.loads(GOLDEN_PATH.read_text())
 
 
 def _model(cuda):
@@ -44,21 +49,21 @@ def _model(cuda):
                               cuda)
 
 
-def test_config2_teacher_forced_256_tokens_match_reference(cuda):
+def test_config2_teacher_forced_256_tokens_match_reference(cuda, golden):
     from nano_infer_engine_b200 import ops
     from nano_infer_engine_b200.paged_cache import PagedKVCache
 
     model = _model(cuda)
     prompts = recipes.config2_prompts()
-    n_new = GOLDEN["new_tokens"]
+    n_new = golden["new_tokens"]
     longest = max(p.shape[1] for p in prompts) + n_new
     cache = PagedKVCache(-(-longest // 16) + 4, 16, 16, 8, 64, torch.bfloat16, cuda)
     matched, total, mismatches = 0, 0, []
     with torch.inference_mode():
         for i, prompt in enumerate(prompts):
             sid = f"req-{i}"
-            ref = GOLDEN["tokens"][sid]
-            margins = GOLDEN["margins"][sid]
+            ref = golden["tokens"][sid]
+            margins = golden["margins"][sid]
             assert len(ref) == len(margins) == n_new
             seq = torch.cat([prompt[0], torch.tensor(ref[:-1])]).to(cuda)
             L = prompt.shape[1]
@@ -81,14 +86,14 @@ def test_config2_teacher_forced_256_tokens_match_reference(cuda):
     assert matched >= MIN_TEACHER_FORCED_MATCHES, report
 
 
-def test_config2_free_running_generation_tracks_reference(cuda):
+def test_config2_free_running_generation_tracks_reference(cuda, golden):
     from nano_infer_engine_b200.generation.config import GenerationConfig
     from nano_infer_engine_b200.generation.scheduler import ContinuousBatchingScheduler
     from nano_infer_engine_b200.paged_cache import PagedKVCache
 
     model = _model(cuda)
     prompts = [p.to(cuda) for p in recipes.config2_prompts()]
-    n_new = GOLDEN["new_tokens"]
+    n_new = golden["new_tokens"]
     blocks = sum(-(-(p.shape[1] + n_new) // 16) for p in prompts) + 16
     cache = PagedKVCache(blocks, 16, 16, 8, 64, torch.bfloat16, cuda)
     config = GenerationConfig(max_new_tokens=n_new, prefill_chunk_size=128, max_prefill_tokens_per_step=512)
@@ -99,8 +104,8 @@ def test_config2_free_running_generation_tracks_reference(cuda):
     agree, firsts = 0, []
     for r in reqs:
         ours = r.sequence[0, r.prompt.shape[1]:].tolist()
-        ref = GOLDEN["tokens"][r.sequence_id]
-        margins = GOLDEN["margins"][r.sequence_id]
+        ref = golden["tokens"][r.sequence_id]
+        margins = golden["margins"][r.sequence_id]
         assert len(ours) == len(ref) == n_new
         k = next((k for k, (a, b) in enumerate(zip(ours, ref)) if a != b), n_new)
         agree += k
