@@ -239,7 +239,7 @@ class PDRank:
     def __init__(self, dist_ctx, rank, world, device, model, host_prompts, new_tokens):
         from nano_infer_engine_b200.generation.pd_disagg import (
             HEADER_WORDS,
-            PairChannel,
+            PipeChannel,
             assign_pairs,
             gpu_import,
             open_peer_pool,
@@ -259,7 +259,8 @@ class PDRank:
         self.host = {i: host_prompts[i] for i in self.mine}
         self.resident = {i: p.to(device) for i, p in self.host.items()}
         longest = max(p.shape[1] for p in host_prompts)
-        self.channel = PairChannel(self.store, rank, self.peer, HEADER_WORDS + -(-longest // 16))
+        # the two ranks of a pair share a node: records go over a pair of named pipes
+        self.channel = PipeChannel(self.store, rank, self.peer, HEADER_WORDS + -(-longest // 16))
         blocks = sum(-(-(self.host[i].shape[1] + (0 if self.prefill else new_tokens)) // 16) for i in self.mine)
         self.cache = PagedKVCache(blocks + 64, 16, 16, 8, 64, torch.bfloat16, device)
         if self.prefill:
@@ -304,6 +305,7 @@ class PDRank:
             close_peer_pool(self.store, self.rank, self.remote)
         else:
             wait_pool_unmapped(self.store, self.peer)
+        self.channel.release()
 
 
 def time_pd(pd, steps, warmup, dist_ctx, e2e=False):
@@ -328,11 +330,23 @@ def time_pd(pd, steps, warmup, dist_ctx, e2e=False):
     return max_over_ranks(dist_ctx, elapsed, pd.device), [int(x) for x in totals.tolist()]
 
 
+def pd_job(pairs, new_tokens):
+    """The closed-loop job for `pairs` P/D pairs: the same seeded 32-request set
+    (config 5's prompt-length distribution) for every pair, interleaved one copy
+    per pair per request.  The least-outstanding-work router then hands every
+    pair one copy of each request, so the per-pair workload is identical at
+    every N (weak scaling on a fixed per-pair job)."""
+    base = pd_workload(2 * PD_REQUESTS_PER_GPU)
+    job = [p for p in base for _ in range(pairs)]
+    return base, job
+
+
 def run_pd(args, dist_ctx, rank, local, device, world):
     """N >= 2 (even): N/2 prefill/decode pairs behind the router, weak scaling
-    (16 requests per GPU), closed loop: one step = every pair generates its batch."""
+    (the same 32-request set per pair), closed loop: one step = every pair generates its batch."""
     model = build_engine(device)
-    host = [p.pin_memory() for p in pd_workload(PD_REQUESTS_PER_GPU * world)]
+    base, job = pd_job(world // 2, args.new_tokens)
+    host = [p.pin_memory() for p in job]
     pd = PDRank(dist_ctx, rank, world, device, model, host, args.new_tokens)
     with ClockSampler(local) as clocks:
         elapsed, (launches, _, _) = time_pd(pd, args.steps, args.warmup, dist_ctx)
@@ -358,10 +372,12 @@ def run_pd(args, dist_ctx, rank, local, device, world):
                     "ms_per_launch": dec["ms"], "peak_kind": f"{peak_kind} (hbm_gbs burst copy)"}
     barrier(dist_ctx)
     if rank == 0:
-        lens = [p.shape[1] for p in host]
+        lens = [p.shape[1] for p in base]
         print(json.dumps({
             "metric": METRIC,
             "value": value,
+            "per_pair": value / (world // 2),
+            "per_gpu": value / world,
             "unit": UNIT,
             "n_gpus": world,
             "steps": args.steps,
@@ -373,8 +389,8 @@ def run_pd(args, dist_ctx, rank, local, device, world):
             "dtype": "bf16",
             "data": "synthetic (seeded prompts, random-init weights N(0, 0.02))",
             "config": {
-                "workload": f"config5 P/D, closed loop: Llama-3.2-1B shape, {PD_REQUESTS_PER_GPU} requests per GPU, "
-                            f"prompts log-normal mean 1024 capped 8192 (sum {sum(lens)}, max {max(lens)}), "
+                "workload": f"config5 P/D, closed loop: Llama-3.2-1B shape, the same {len(base)} requests per pair "
+                            f"(prompts log-normal mean 1024 capped 8192, per pair sum {sum(lens)}, max {max(lens)}), "
                             f"{args.new_tokens} greedy new tokens; prefill batches <=4096 tokens; KV blocks pulled "
                             "over NVLink by the decode GPU",
                 "global_batch": len(host),

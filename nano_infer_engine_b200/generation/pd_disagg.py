@@ -102,6 +102,114 @@ class PairChannel:
         """Messages are delivered when ``send`` returns; nothing is left in flight."""
 
 
+class PipeChannel:
+    """The same ordered int64 messages as :class:`PairChannel`, over two named
+    pipes (one per direction) between the ranks of a pair on one node.
+
+    A poll is one non-blocking ``read`` (no round trip to the store's server).
+    Each pipe has one writer, so the byte stream keeps the records in order
+    even when a write is partial; bytes the pipe cannot take yet wait in a
+    local queue that every ``send`` and ``poll`` retries (neither side ever
+    blocks on a full pipe, so the pair cannot deadlock).  Set-up: the lower
+    rank of the pair creates the pipes in a fresh temporary directory and
+    publishes its path in the store; both ends open non-blocking.
+    """
+
+    def __init__(self, store, me: int, peer: int, words: int, *, timeout_s: float = 60.0) -> None:
+        import os
+        import tempfile
+
+        self.words = words
+        self.bytes = 8 * words
+        key = f"pd/pipe/{min(me, peer)}-{max(me, peer)}"
+        if me < peer:
+            self._dir = tempfile.mkdtemp(prefix="nie_pd_")
+            for a, b in ((me, peer), (peer, me)):
+                os.mkfifo(os.path.join(self._dir, f"{a}to{b}"))
+            store.set(key, self._dir.encode())
+        else:
+            store.wait([key])
+            self._dir = store.get(key).decode()
+        self._os = os
+        # open the read end first, non-blocking: opening a write end without a
+        # reader fails with ENXIO, so retry it (bounded) until the peer's read end exists
+        self._rfd = os.open(os.path.join(self._dir, f"{peer}to{me}"), os.O_RDONLY | os.O_NONBLOCK)
+        wpath = os.path.join(self._dir, f"{me}to{peer}")
+        deadline = time.monotonic() + timeout_s
+        while True:
+            try:
+                self._wfd = os.open(wpath, os.O_WRONLY | os.O_NONBLOCK)
+                break
+            except OSError:
+                if time.monotonic() > deadline:
+                    raise TimeoutError(f"pair channel: peer {peer} never opened its end")
+                time.sleep(0.001)
+        self._owner = me < peer
+        self._pending: deque[bytes] = deque()
+        self._buf = b""
+
+    def _flush(self) -> None:
+        while self._pending:
+            try:
+                n = self._os.write(self._wfd, self._pending[0])
+            except BlockingIOError:
+                return
+            if n < len(self._pending[0]):
+                self._pending[0] = self._pending[0][n:]  # the rest follows in stream order
+                return
+            self._pending.popleft()
+
+    def send(self, values: list[int]) -> None:
+        if len(values) > self.words:
+            raise ValueError("message longer than the channel's fixed size")
+        msg = np.zeros(self.words, dtype=np.int64)
+        msg[: len(values)] = values
+        self._pending.append(msg.tobytes())
+        self._flush()
+
+    def poll(self, stop_after: int | None = None) -> list[list[int]]:
+        """Every waiting message in order; with ``stop_after``, none past the first
+        message of that type (later ones stay buffered, e.g. the next pass's)."""
+        self._flush()
+        while True:
+            try:
+                chunk = self._os.read(self._rfd, 1 << 16)
+            except BlockingIOError:
+                break
+            if not chunk:
+                break
+            self._buf += chunk
+        out = []
+        while len(self._buf) >= self.bytes:
+            out.append(np.frombuffer(self._buf[: self.bytes], dtype=np.int64).tolist())
+            self._buf = self._buf[self.bytes:]
+            if stop_after is not None and out[-1][0] == stop_after:
+                break
+        return out
+
+    def close(self) -> None:
+        """Deliver whatever is still queued (bounded), then release the pipes."""
+        deadline = time.monotonic() + 60.0
+        while self._pending and time.monotonic() < deadline:
+            self._flush()
+            if self._pending:
+                time.sleep(0.0005)
+        if self._pending:
+            raise TimeoutError("pair channel: the peer stopped reading")
+
+    def release(self) -> None:
+        """Close both descriptors; the creating rank removes the pipes."""
+        import shutil
+
+        for fd in (self._rfd, self._wfd):
+            try:
+                self._os.close(fd)
+            except OSError:
+                pass
+        if self._owner:
+            shutil.rmtree(self._dir, ignore_errors=True)
+
+
 @dataclass
 class RemotePool:
     """The prefill rank's KV pool as mapped into the decode process."""

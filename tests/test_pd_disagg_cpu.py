@@ -1,9 +1,10 @@
 """P/D disaggregation protocol across two processes (gloo, CPU, scripted models).
 
-Rank 0 prefills and hands requests off through the TCP store; rank 1 imports (host bookkeeping
+Rank 0 prefills and hands requests off; rank 1 imports (host bookkeeping
 only here), decodes with continuous batching and acknowledges; the prefill
-rank frees each request's blocks on the acknowledgement.  The GPU copy path
-is exercised by tests/test_pd_gpu.py.
+rank frees each request's blocks on the acknowledgement.  The records travel
+through the TCP store (PairChannel) or a pair of named pipes (PipeChannel).
+The GPU copy path is exercised by tests/test_pd_gpu.py.
 """
 
 import socket
@@ -18,6 +19,7 @@ from nano_infer_engine_b200.generation.config import GenerationConfig
 from nano_infer_engine_b200.generation.pd_disagg import (
     HEADER_WORDS,
     PairChannel,
+    PipeChannel,
     assign_pairs,
     run_decode,
     run_prefill,
@@ -58,14 +60,59 @@ def test_pair_channel_order_and_pass_boundary():
         a.send([0] * (HEADER_WORDS + 1))
 
 
-def _worker(rank, port, result_path):
+N_PIPE = 256
+PIPE_WORDS = 600  # 4800-byte records: larger than the pipe's atomic write size, so writes split
+
+
+def _pipe_order_worker(rank, port, result_path):
+    store = dist.TCPStore("127.0.0.1", port, 2, rank == 0, timeout=timedelta(seconds=60))
+    ch = PipeChannel(store, rank, 1 - rank, PIPE_WORDS)
+    got = []
+    if rank == 0:
+        for i in range(N_PIPE):  # 1.2 MB, far more than a pipe holds: the rest waits in the sender's queue
+            ch.send([1, i])
+        ch.send([3, N_PIPE])
+        ch.send([1, N_PIPE + 1])
+        ch.close()
+        while not got:
+            got = ch.poll()
+    else:
+        import time
+
+        while len(got) < N_PIPE + 1:
+            got += ch.poll(stop_after=3)
+            time.sleep(0.0005)
+        rest = []
+        while not rest:
+            rest = ch.poll()
+        got.append(rest)
+        ch.send([2, 9])
+        ch.close()
+    torch.save(got, f"{result_path}.{rank}")
+    store.set(f"done/{rank}", b"1")
+    store.wait([f"done/{1 - rank}"])
+    ch.release()
+
+
+def test_pipe_channel_order_backpressure_and_pass_boundary(tmp_path):
+    path = str(tmp_path / "pipe")
+    mp.start_processes(_pipe_order_worker, args=(_free_port(), path), nprocs=2, start_method="spawn", join=True)
+    pad = [0] * (PIPE_WORDS - 2)
+    recv = torch.load(path + ".1")
+    assert recv[:N_PIPE] == [[1, i, *pad] for i in range(N_PIPE)]
+    assert recv[N_PIPE] == [3, N_PIPE, *pad]  # stopped after the pass boundary
+    assert recv[N_PIPE + 1] == [[1, N_PIPE + 1, *pad]]  # the next pass's record was kept
+    assert torch.load(path + ".0") == [[2, 9, *pad]]
+
+
+def _worker(rank, port, result_path, kind="store"):
     from test_scheduler_host import ScriptedModel
 
     store = dist.TCPStore("127.0.0.1", port, 2, rank == 0, timeout=timedelta(seconds=60))
     dist.init_process_group("gloo", store=store, rank=rank, world_size=2, timeout=timedelta(seconds=60))
     prompts = _prompts()
     words = HEADER_WORDS + 16
-    channel = PairChannel(store, rank, 1 - rank, words)
+    channel = (PipeChannel if kind == "pipe" else PairChannel)(store, rank, 1 - rank, words)
     schedules = {f"pd-{i}": tuple(range(1, 8)) for i in range(len(prompts))}
     if rank == 0:
         cache = PagedKVCache(16, 4, 1, 1, 4, torch.float32, "cpu")  # 16 blocks: forces waiting for ACKs
@@ -97,6 +144,8 @@ def _worker(rank, port, result_path):
         }
     torch.save(result, f"{result_path}.{rank}")
     dist.barrier()
+    if kind == "pipe":
+        channel.release()
     dist.destroy_process_group()
 
 
@@ -106,9 +155,10 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_prefill_decode_handoff_over_gloo(tmp_path):
+@pytest.mark.parametrize("kind", ["store", "pipe"])
+def test_prefill_decode_handoff_over_gloo(tmp_path, kind):
     path = str(tmp_path / "res")
-    mp.start_processes(_worker, args=(_free_port(), path), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_worker, args=(_free_port(), path, kind), nprocs=2, start_method="spawn", join=True)
     pre = torch.load(path + ".0")
     dec = torch.load(path + ".1")
     assert pre["requests"] == len(PROMPT_LENS)
