@@ -4,14 +4,17 @@
 // Work decomposition (persistent, stream-K).  A "segment" is one (128-query
 // tile of one request, query head) pair; it owns ceil(keys / 64) key tiles.
 // All segments are laid end to end (query tile major, head minor, so the
-// heads sharing a kv head are neighbours) and the resulting list of key tiles
-// is cut into equal contiguous ranges, one per CTA, with two CTAs per SM and
-// one wave: every SM does the same amount of tile work whatever the length
-// mix, and each CTA pays its prologue once.  A segment that lies wholly in
-// one CTA's range is normalised and written by that CTA; a segment cut by a
-// range boundary leaves (max, sum, unnormalised O) partials in one of two
-// slots of each CTA it touches, which prefill_combine_kernel merges in CTA
-// order.  Without a workspace each CTA takes exactly one segment instead.
+// heads sharing a kv head are neighbours), each weighted as its key tiles plus
+// kPfSegCost for its fixed work (first and diagonal tiles, epilogue, pipeline
+// drain), and the resulting cost list is cut into equal contiguous ranges,
+// one per CTA, with two CTAs per SM and one wave: every SM does the same
+// amount of work whatever the length mix (short segments cost more per tile),
+// and each CTA pays its prologue once.  A segment that lies wholly in one
+// CTA's range is normalised and written by that CTA; a segment cut by a range
+// boundary leaves (max, sum, unnormalised O) partials in one of two slots of
+// each CTA it touches, which prefill_combine_kernel (a dependent launch)
+// merges in CTA order.  Without a workspace each CTA takes exactly one
+// segment instead.
 //
 // Roles of the 6 warps of a CTA (all iterate the same segments / tiles):
 //   warp 4  TMA producer   per segment the Q tile (128 rows x 128 B) into one
@@ -25,12 +28,14 @@
 //                          (M=128, N=64, 4 x K=16, A = P read from TMEM, V as
 //                          an MN-major operand) into the segment's TMEM O
 //                          buffer (two O buffers alternate between segments).
-//   warps 0-3 softmax      thread t owns query row t: one pass over its S row
-//                          (64 values in registers): reference rounding
+//   warps 0-3 softmax      thread t owns query row t: its S row (64 values
+//                          in registers) rounded as the reference does
 //                          (score = bf16(bf16(q.k) * scale); exact as one
-//                          rounding when scale is a power of two), causal mask
-//                          on diagonal tiles only, row max, exp2, row sum, P
-//                          as bf16 pairs written over the S columns.  The
+//                          rounding when scale is a power of two) straight
+//                          into bf16 pairs, causal mask on diagonal tiles
+//                          only, row max on the pairs (max.bf16x2), exp2
+//                          arguments and row sums two lanes per instruction
+//                          (f32x2), P as bf16 pairs over the S columns.  The
 //                          running max is only raised when a tile exceeds it
 //                          by more than 2^8 (lazy rescale: O in TMEM and l are
 //                          then scaled once); otherwise P is taken against the
@@ -60,10 +65,14 @@ constexpr int kPfBlockBytes = kPfBS * kPfHD * 2;  // 2 KiB
 constexpr uint32_t kSCol0 = 0, kSCol1 = 64, kOCol0 = 128;  // O buffer b at kOCol0 + 64 b
 constexpr float kPfLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;
+// Work of one segment beyond its key tiles (first tile, diagonal tiles, the
+// O epilogue, the pipeline drain and refill), in key tiles: the persistent
+// grid splits key tiles plus this much per segment evenly over the CTAs.
+constexpr int kPfSegCost = 3;
 constexpr int kPfMaxUnits = 2048;  // 128-query tiles per call (larger calls use the generic kernel)
 constexpr int kPfMaxCtas = 320;    // persistent grid bound (2 per SM)
 constexpr int kPfPartialFloats = (2 + kPfHD) * kPfBM;  // m[128], l[128], O[64][128]
-// workspace: [cum: kPfMaxUnits + 2 int32 (tile prefix sums, then W) | partials]
+// workspace: [cum: kPfMaxUnits + 2 int32 (cost prefix sums, then W) | partials]
 constexpr size_t kPfCumBytes = ((size_t)(kPfMaxUnits + 2) * sizeof(int32_t) + 255) & ~size_t(255);
 
 struct PrefillArgs {
@@ -116,11 +125,33 @@ __device__ __forceinline__ bool pf_wait(PfBars* b, uint64_t* bar, uint32_t parit
   return false;
 }
 
-// Round two fp32 values to bf16 and back (one packed conversion).
-__device__ __forceinline__ void round_bf16_pair(float& a, float& b) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  a = __low2float(h);
-  b = __high2float(h);
+// The two halves of a bf16 pair as fp32 (exact).
+__device__ __forceinline__ float bf16_lo(uint32_t r) { return __uint_as_float(r << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t r) { return __uint_as_float(r & 0xffff0000u); }
+
+// Lane-wise maximum of two bf16 pairs (exact, as the fp32 maximum of the values).
+__device__ __forceinline__ uint32_t max_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// d = a * b + c on two fp32 lanes in one instruction (sm_100 f32x2): each lane
+// is an IEEE fma, so the results equal two fmaf calls.
+__device__ __forceinline__ void fma_f32x2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                          float c1) {
+  asm("{\n.reg .b64 ra, rb, rc, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+      "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+// d += b on two fp32 lanes in one instruction.
+__device__ __forceinline__ void add_f32x2(float& d0, float& d1, float b0, float b1) {
+  asm("{\n.reg .b64 ra, rb, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "add.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(d0), "f"(d1), "f"(b0), "f"(b1));
 }
 
 // Geometry of one 128-query tile ("unit").
@@ -148,39 +179,52 @@ __device__ __forceinline__ PfUnit pf_unit(const PrefillArgs& a, int u) {
   return x;
 }
 
-// Walks the segments that overlap this CTA's key-tile range [lo, hi) of the
-// global list; identical in every warp.  cum[u] = key tiles of units < u.
+// Cost of a unit per query head: its key tiles plus kPfSegCost when it has any.
+__device__ __forceinline__ int pf_unit_cost(int n_kt) { return n_kt > 0 ? n_kt + kPfSegCost : 0; }
+
+// The global work list: segments (unit major, head minor), each occupying a
+// cost interval of kPfSegCost followed by its key tiles; cum[u] = the cost of
+// one head of every unit < u, so segment (u, h) starts at hq cum[u] + h d_u
+// with d_u = cum[u + 1] - cum[u].  A CTA owns the cost range [lo, hi) and
+// processes the key tiles that lie in it.  Walks the segments with tiles in
+// that range; identical in every warp.
 struct PfSegIter {
   const int* cum;
   int units, hq;
   int64_t lo, hi;
   int u, h;        // current segment
-  int64_t start;   // its first global tile
+  int d;           // cost of one segment of unit u
+  int64_t start;   // cost position of its first key tile
   int n;           // its key tiles
 
+  __device__ void set_unit() {
+    d = cum[u + 1] - cum[u];
+    n = d > 0 ? d - kPfSegCost : 0;
+  }
   __device__ void init(const int* c, int U, int H, int64_t a_lo, int64_t a_hi) {
     cum = c;
     units = U;
     hq = H;
     lo = a_lo;
     hi = a_hi;
-    // largest unit with hq * cum[u] <= lo (it has tiles since lo < total)
+    // largest unit with hq * cum[u] <= lo (it has cost since lo < total)
     int l = 0, r = U - 1;
     while (l < r) {
       const int m = (l + r + 1) >> 1;
       if ((int64_t)hq * cum[m] <= lo) l = m; else r = m - 1;
     }
     u = l;
-    n = cum[u + 1] - cum[u];
-    h = n > 0 ? (int)((lo - (int64_t)hq * cum[u]) / n) : 0;
-    start = (int64_t)hq * cum[u] + (int64_t)h * n;
+    set_unit();
+    h = d > 0 ? (int)((lo - (int64_t)hq * cum[u]) / d) : 0;
+    start = (int64_t)hq * cum[u] + (int64_t)h * d + kPfSegCost;
   }
+  // a segment whose tiles start at or past hi belongs to the next CTA
   __device__ bool valid() const { return lo < hi && start < hi; }
   __device__ int t_lo() const { return (int)(max(lo, start) - start); }
   __device__ int t_hi() const { return (int)(min(hi, start + n) - start); }
   __device__ void next() {
     if (++h < hq) {
-      start += n;
+      start += d;
       return;
     }
     h = 0;
@@ -191,8 +235,8 @@ struct PfSegIter {
       start = hi;
       return;
     }
-    n = cum[u + 1] - cum[u];
-    start = (int64_t)hq * cum[u];
+    set_unit();
+    start = (int64_t)hq * cum[u] + kPfSegCost;
   }
 };
 
@@ -207,13 +251,13 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int U = a.units;
 
-  // ---- key tiles per unit and their prefix sums (the whole CTA)
+  // ---- cost per unit and head, and their prefix sums (the whole CTA)
   {
     const int per = (U + kPfThreads - 1) / kPfThreads;
     const int u0 = threadIdx.x * per, u1 = min(U, u0 + per);
     int local = 0;
     for (int u = u0; u < u1; ++u) {
-      const int n = pf_unit(a, u).n_kt;
+      const int n = pf_unit_cost(pf_unit(a, u).n_kt);
       b->cum[u] = n;
       local += n;
     }
@@ -251,10 +295,12 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   } else {
     // one segment per CTA: blockIdx.x = unit * hq + head
     const int u = blockIdx.x / a.hq, h = blockIdx.x % a.hq;
-    const int n = b->cum[u + 1] - b->cum[u];
-    lo = (int64_t)a.hq * b->cum[u] + (int64_t)h * n;
-    hi = lo + n;
+    const int d = b->cum[u + 1] - b->cum[u];
+    lo = (int64_t)a.hq * b->cum[u] + (int64_t)h * d;
+    hi = lo + d;
   }
+  // the combine kernel may be staged now: it waits for this grid to complete
+  pdl_trigger();
   if (lo >= hi) return;  // uniform: nothing to do for this CTA
 
   if (threadIdx.x == 0) {
@@ -447,6 +493,9 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     bool ok = true;
     uint32_t v[64];
+    // exp2 argument per unit of the stored score: the stored scores are raw
+    // (scale not applied) when the scale is a power of two
+    const float coef = a.scale_pow2 ? a.scale_log2e : kPfLog2e;
     int k = 0;
     int64_t g = 0;
     for (; ok && seg.valid(); seg.next(), ++k) {
@@ -468,51 +517,40 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         tmem_ld32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_wait_ld();
-        const int key0 = kt * kPfBN;
-        const bool masked = key0 + kPfBN - 1 > diag_from;
-        // v holds the rounded scores in the "raw" domain (before * scale*log2e,
-        // a positive factor, so the max can be taken before scaling); eight
-        // independent max chains
-        float mxa[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mxa[i] = -INFINITY;
+        // r[e]: the rounded scores of keys 2e, 2e+1 as a bf16 pair.  With a
+        // power-of-two scale bf16(bf16(acc) * 2^k) == bf16(acc) * 2^k, so one
+        // rounding gives the raw-domain score and the scale rides in coef;
+        // otherwise r holds bf16(bf16(acc) * scale) itself.
+        uint32_t r[32];
         if (a.scale_pow2) {
-          // bf16(bf16(acc) * 2^k) == bf16(acc) * 2^k: one rounding
 #pragma unroll
-          for (int e = 0; e < 64; e += 2) {
-            float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
-            round_bf16_pair(x0, x1);
-            if (masked) {
-              if (key0 + e > qpos) x0 = -INFINITY;
-              if (key0 + e + 1 > qpos) x1 = -INFINITY;
-            }
-            v[e] = __float_as_uint(x0);
-            v[e + 1] = __float_as_uint(x1);
-            mxa[(e >> 1) & 7] = fmaxf(mxa[(e >> 1) & 7], fmaxf(x0, x1));
-          }
+          for (int e = 0; e < 32; ++e) r[e] = pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
         } else {
-          // bf16(bf16(acc) * scale), kept in the raw domain
 #pragma unroll
-          for (int e = 0; e < 64; e += 2) {
-            float x0 = __uint_as_float(v[e]), x1 = __uint_as_float(v[e + 1]);
-            round_bf16_pair(x0, x1);
-            x0 *= a.scale;
-            x1 *= a.scale;
-            round_bf16_pair(x0, x1);
-            x0 /= a.scale;  // exact: undoes a multiply whose result is representable
-            x1 /= a.scale;
-            if (masked) {
-              if (key0 + e > qpos) x0 = -INFINITY;
-              if (key0 + e + 1 > qpos) x1 = -INFINITY;
-            }
-            v[e] = __float_as_uint(x0);
-            v[e + 1] = __float_as_uint(x1);
-            mxa[(e >> 1) & 7] = fmaxf(mxa[(e >> 1) & 7], fmaxf(x0, x1));
+          for (int e = 0; e < 32; ++e) {
+            const uint32_t h = pack_bf16x2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
+            r[e] = pack_bf16x2(bf16_lo(h) * a.scale, bf16_hi(h) * a.scale);
           }
         }
-        const float mx_raw = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                                   fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
-        const float mx = mx_raw * a.scale_log2e;
+        const int key0 = kt * kPfBN;
+        if (key0 + kPfBN - 1 > diag_from) {
+          // causal mask (diagonal tiles only): keys past the row's position
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            if (key0 + 2 * e > qpos) r[e] = (r[e] & 0xffff0000u) | 0xff80u;
+            if (key0 + 2 * e + 1 > qpos) r[e] = (r[e] & 0x0000ffffu) | 0xff800000u;
+          }
+        }
+        // row max of the bf16 scores (coef > 0, so it is taken before scaling):
+        // eight independent packed chains
+        uint32_t mx2[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx2[i] = r[i];
+#pragma unroll
+        for (int e = 8; e < 32; ++e) mx2[e & 7] = max_bf16x2(mx2[e & 7], r[e]);
+        const uint32_t mxp = max_bf16x2(max_bf16x2(max_bf16x2(mx2[0], mx2[1]), max_bf16x2(mx2[2], mx2[3])),
+                                        max_bf16x2(max_bf16x2(mx2[4], mx2[5]), max_bf16x2(mx2[6], mx2[7])));
+        const float mx = fmaxf(bf16_lo(mxp), bf16_hi(mxp)) * coef;
         const bool raise = mx > m_ref + kRescaleLog2;
         if (__any_sync(0xffffffffu, raise)) {
           const float alpha = raise ? fast_exp2(m_ref - mx) : 1.f;
@@ -542,24 +580,26 @@ __global__ void __launch_bounds__(kPfThreads, 2)
             }
           }
         }
-        float rsa[8];
+        // p = exp2(score * coef - m_ref) two lanes at a time; a row whose keys
+        // in this range are all masked keeps m_ref = -inf: its p must come out
+        // 0, not exp2(-inf + inf)
+        float rs[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) rsa[i] = 0.f;
+        for (int i = 0; i < 8; ++i) rs[i] = 0.f;
+        const float neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
         uint32_t pk[32];
-        // a row whose keys in this range are all masked keeps m_ref = -inf:
-        // its p must come out 0, not exp2(-inf + inf)
-        const float sl2e = a.scale_log2e, neg_m = (m_ref == -INFINITY) ? 0.f : -m_ref;
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(v[2 * e]), sl2e, neg_m));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(v[2 * e + 1]), sl2e, neg_m));
-          rsa[e & 7] += p0 + p1;
+          float y0, y1;
+          fma_f32x2(y0, y1, bf16_lo(r[e]), bf16_hi(r[e]), coef, coef, neg_m, neg_m);
+          const float p0 = fast_exp2(y0), p1 = fast_exp2(y1);
+          add_f32x2(rs[2 * (e & 3)], rs[2 * (e & 3) + 1], p0, p1);
           pk[e] = pack_bf16x2(p0, p1);
         }
-        const float rs = ((rsa[0] + rsa[1]) + (rsa[2] + rsa[3])) + ((rsa[4] + rsa[5]) + (rsa[6] + rsa[7]));
+        const float row_sum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
         tmem_st32(s_addr, pk);
         tmem_wait_st();
-        l += rs;
+        l += row_sum;
         tc_fence_before();
         mbar_arrive(&b->p_full[sb]);
       }
@@ -611,15 +651,21 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 }
 
 // Merge the partials of segments that were cut across CTAs (stream mode).
-// grid = (units, q_heads), one thread per query row.
+// grid = (units, q_heads, kPfCombineSplit), one thread per query row and
+// kPfHD / kPfCombineSplit head dimensions.  Launched as a dependent of the
+// attention kernel: it reads nothing before pdl_wait().
+constexpr int kPfCombineSplit = 4;
+constexpr int kPfCombineD = kPfHD / kPfCombineSplit;
 __global__ void __launch_bounds__(kPfBM) prefill_combine_kernel(PrefillArgs a) {
-  const int u = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+  pdl_wait();
+  const int u = blockIdx.x, h = blockIdx.y, t = threadIdx.x, d0 = blockIdx.z * kPfCombineD;
   const int32_t* cum = a.cum_out;
-  const int n = cum[u + 1] - cum[u];
+  const int d = cum[u + 1] - cum[u];
   const int64_t W = cum[kPfMaxUnits + 1];
-  if (n == 0 || W <= 0) return;
-  const int64_t s0 = (int64_t)a.hq * cum[u] + (int64_t)h * n, s1 = s0 + n;
-  const int64_t c0 = s0 / W, c1 = (s1 - 1) / W;
+  if (d == 0 || W <= 0) return;
+  // the segment's cost interval starts at s0; its key tiles occupy [s1, s2)
+  const int64_t s0 = (int64_t)a.hq * cum[u] + (int64_t)h * d, s1 = s0 + kPfSegCost, s2 = s0 + d;
+  const int64_t c0 = s1 / W, c1 = (s2 - 1) / W;  // the CTAs that processed its tiles
   if (c0 == c1) return;  // written directly by its CTA
   const PfUnit x = pf_unit(a, u);
   if (t >= x.nq) return;
@@ -630,21 +676,21 @@ __global__ void __launch_bounds__(kPfBM) prefill_combine_kernel(PrefillArgs a) {
   float M = -INFINITY;
   for (int64_t c = c0; c <= c1; ++c) M = fmaxf(M, slot(c)[t]);
   float L = 0.f;
-  float o[kPfHD];
+  float o[kPfCombineD];
 #pragma unroll
-  for (int d = 0; d < kPfHD; ++d) o[d] = 0.f;
+  for (int j = 0; j < kPfCombineD; ++j) o[j] = 0.f;
   for (int64_t c = c0; c <= c1; ++c) {
     const float* ps = slot(c);
     const float m = ps[t];
     const float w = (m == -INFINITY) ? 0.f : fast_exp2(m - M);
     L += ps[kPfBM + t] * w;
 #pragma unroll
-    for (int d = 0; d < kPfHD; ++d) o[d] += ps[2 * kPfBM + d * kPfBM + t] * w;
+    for (int j = 0; j < kPfCombineD; ++j) o[j] += ps[2 * kPfBM + (d0 + j) * kPfBM + t] * w;
   }
   const float inv = 1.f / L;
-  __nv_bfloat16* op = a.out + (x.qs + x.q0 + t) * a.out_stride + (int64_t)h * kPfHD;
+  __nv_bfloat16* op = a.out + (x.qs + x.q0 + t) * a.out_stride + (int64_t)h * kPfHD + d0;
 #pragma unroll
-  for (int c = 0; c < kPfHD / 8; ++c) {
+  for (int c = 0; c < kPfCombineD / 8; ++c) {
     uint4 w;
     w.x = pack_bf16x2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
     w.y = pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
@@ -749,7 +795,7 @@ int launch_prefill_tc(const void* q, void* out, int64_t row_stride, int64_t num_
   prefill_tc_kernel<<<grid, kPfThreads, smem, s>>>(qmap, kmap, vmap, pa);
   int rc = check_launch("prefill_tc_kernel");
   if (rc != NIE_OK || !pa.stream) return rc;
-  prefill_combine_kernel<<<dim3((unsigned)units, (unsigned)q_heads), kPfBM, 0, s>>>(pa);
+  pdl_launch(prefill_combine_kernel, dim3((unsigned)units, (unsigned)q_heads, kPfCombineSplit), dim3(kPfBM), s, pa);
   return check_launch("prefill_combine_kernel");
 }
 
