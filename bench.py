@@ -270,6 +270,10 @@ class PDRank:
             self.remote = open_peer_pool(self.store, self.peer, self.cache)
             self.transfers = []
             self.pull = gpu_import(self.remote, self.transfers)
+            # decode graphs for batch sizes up to graph_batches are captured during
+            # the first (warm-up) pass, on a block table sized once for every run
+            self.graph_batches = min(64, len(self.mine))
+            self.cache.reserve_table(len(self.mine) + 8, -(-model.config.max_seq_len // 16))
 
     def step(self, e2e=False, indices=None, arrival=None, clock=time.perf_counter, record=None):
         """One pass over this pair's requests (``indices``: a subset, in order);
@@ -292,7 +296,8 @@ class PDRank:
             return h2d, 0, None
         reqs = run_decode(self.model, self.cache, self.channel, prompts.__getitem__,
                           GenerationConfig(max_new_tokens=self.new_tokens), len(mine), self.pull,
-                          self.model.config.vocab_size, idle_sleep=0.0002, clock=clock, timings=record)
+                          self.model.config.vocab_size, idle_sleep=0.0002, clock=clock, timings=record,
+                          graph_batches=self.graph_batches)
         if e2e:
             outs = [r.sequence.to("cpu") for r in reqs]
             return h2d, sum(o.numel() * o.element_size() for o in outs), outs
@@ -432,13 +437,15 @@ def run_pd_open(args, dist_ctx, rank, local, device, world):
         if not pd.prefill:
             pd.transfers.clear()
         torch.cuda.synchronize()
-        barrier(dist_ctx)
-        t0 = time.monotonic()
         record = {}
         with ClockSampler(local) as clocks:
+            # the sampler is up before the clock starts: arrivals, first tokens
+            # and completions all use this rank's clock from t0
+            barrier(dist_ctx)
+            t0 = time.monotonic()
             pd.step(arrival=arrival, clock=lambda: time.monotonic() - t0, record=record)
-        torch.cuda.synchronize()
-        elapsed = time.monotonic() - t0
+            torch.cuda.synchronize()
+            elapsed = time.monotonic() - t0
     elapsed = max_over_ranks(dist_ctx, elapsed, device)
     # gather per-request timings and transfer records on rank 0 through the store
     store = dist_ctx.distributed_c10d._get_default_store()

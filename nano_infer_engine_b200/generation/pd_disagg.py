@@ -324,16 +324,16 @@ def run_prefill(
 
     Batches are formed from arrived requests up to ``token_budget`` prompt
     tokens and the free blocks of ``cache``; a request's blocks are held
-    until the decode peer acknowledges its copy.  ``arrival`` (seconds from
-    the start, same order as ``requests``) gates admission for open-loop runs;
+    until the decode peer acknowledges its copy.  ``arrival`` (``clock()``
+    times, same order as ``requests``) gates admission for open-loop runs;
     ``first_token_at`` receives, per request index, the ``clock()`` time at
-    which its first token was known.
+    which its first token was known, so TTFT = first_token_at - arrival on one
+    time base.
     """
     stats = PrefillStats()
     pending = deque(range(len(requests)))
     held: dict[int, str] = {}
     bs = cache.block_size
-    start = clock()
     while pending or held:
         for msg in channel.poll():
             if msg[0] == ACK:
@@ -341,7 +341,7 @@ def run_prefill(
         batch: list[int] = []
         tokens = 0
         blocks = 0
-        now = clock() - start
+        now = clock()
         while pending:
             k = pending[0]
             if arrival is not None and arrival[k] > now:
@@ -395,11 +395,16 @@ def run_decode(
     idle_sleep: float = 0.0,
     clock: Callable[[], float] = time.perf_counter,
     timings: dict[int, tuple[float, float]] | None = None,
+    graph_batches: int = 0,
 ) -> list[PagedRequest]:
     """Receive hand-offs, import their KV, and decode them with continuous batching.
 
     ``timings`` receives, per request index, the ``clock()`` times at which
-    its hand-off arrived and at which it completed.
+    its hand-off arrived and at which it completed.  With ``graph_batches``
+    the decode graphs of batch sizes 1 .. graph_batches are captured after
+    the first decode step (the block table first sized for ``max_batch_size``
+    sequences of the model's longest length), so that a batch size seen later
+    does not stall its step with a capture.
     """
     sched = ContinuousBatchingScheduler(model, config, cache, max_batch_size)
     ready: deque[tuple[PagedRequest, torch.Tensor]] = deque()
@@ -438,6 +443,10 @@ def run_decode(
             requests.append(request)
         if sched.has_work:
             out = sched.step()
+            if graph_batches and hasattr(model, "capture_decode_graphs"):
+                cache.reserve_table(max_batch_size, -(-model.config.max_seq_len // bs))
+                model.capture_decode_graphs(cache, range(1, graph_batches + 1))
+                graph_batches = 0
             if timings is not None and out.terminal_requests:
                 now = clock()
                 for r in out.terminal_requests:

@@ -334,6 +334,29 @@ class Llama3_2(nn.Module):
             self.__dict__["_fused_sig"] = (first.attn.q_proj.weight.data_ptr(), last.ffn.up_proj.weight.data_ptr())
         return self.__dict__.get("_weights_gen", 0)
 
+    def capture_decode_graphs(self, cache: PagedKVCache, batches) -> int:
+        """Capture the decode-step graphs of the given batch sizes ahead of use.
+
+        A batch size seen for the first time otherwise runs eagerly and is
+        captured on the spot, stalling every request of that step.  Call after
+        at least one step has run on this model (library handles and fused
+        weights exist), with the cache's block table already sized by
+        ``PagedKVCache.reserve_table`` (growing it retires the graphs).
+        Returns the number of graphs captured.
+        """
+        table = cache.device_block_tables()
+        graphs = cache.__dict__.setdefault("_decode_graphs", {})
+        generation = self._ensure_fused()
+        made = 0
+        for batch in batches:
+            key = (id(self), batch)
+            graph = graphs.get(key)
+            if graph is not None and graph.table is table and graph.generation == generation:
+                continue
+            graphs[key] = _DecodeGraph(self, cache, batch)
+            made += 1
+        return made
+
     def _decode_step(
         self,
         input_ids: torch.Tensor,

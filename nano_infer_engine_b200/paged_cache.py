@@ -198,6 +198,13 @@ class PagedKVCache:
         self._table_dev = None
         self._table_dirty = True
 
+    def reserve_table(self, rows: int, cols: int) -> None:
+        """Size the block-table mirror for ``rows`` live sequences of up to
+        ``cols`` blocks each, so that it is not reallocated while they run
+        (a reallocation retires every captured decode graph of this cache)."""
+        if rows > self._table_host.shape[0] or cols > self._table_host.shape[1]:
+            self._grow_table(rows=rows, cols=cols)
+
     def _store_row_entries(self, sequence_id: str, start: int, ids: list[int]) -> None:
         end = start + len(ids)
         if end > self._table_host.shape[1]:

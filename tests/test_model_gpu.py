@@ -127,6 +127,44 @@ def _generate(model, cfg, prompts, cuda, *, graphs, chunk):
     return [r.sequence[0].tolist() for r in reqs], logits, cache
 
 
+def test_precaptured_decode_graphs_match_eager_and_no_step_captures(cuda, monkeypatch):
+    """Graphs captured ahead (table reserved first) serve every later decode step: same tokens as eager."""
+    from nano_infer_engine_b200 import ops
+    from nano_infer_engine_b200.generation.config import GenerationConfig
+    from nano_infer_engine_b200.generation.scheduler import ContinuousBatchingScheduler
+    from nano_infer_engine_b200.models import llama
+    from nano_infer_engine_b200.paged_cache import PagedKVCache
+
+    model, cfg = _llama_shaped_model(cuda)
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg.vocab_size, (1, n), generator=g).to(cuda) for n in (9, 33, 70, 18)]
+    eager_tokens, _, _ = _generate(model, cfg, prompts, cuda, graphs=False, chunk=None)
+
+    model.cuda_graphs = True
+    cache = PagedKVCache(256, 16, cfg.num_layers, cfg.kv_head_num, cfg.head_dim, torch.bfloat16, cuda)
+    sched = ContinuousBatchingScheduler(model, GenerationConfig(max_new_tokens=12), cache, 4)
+    reqs = [sched.add_request(f"r{i}", p) for i, p in enumerate(prompts)]
+    captured = []
+    original = llama._DecodeGraph.__init__
+
+    def counting(self, *args):
+        captured.append(args[-1])
+        original(self, *args)
+
+    monkeypatch.setattr(llama._DecodeGraph, "__init__", counting)
+    with torch.inference_mode():
+        sched.step()  # the first step initialises the library handles
+        cache.reserve_table(8, -(-cfg.max_seq_len // 16))
+        assert model.capture_decode_graphs(cache, range(1, 5)) == 4
+        assert model.capture_decode_graphs(cache, range(1, 5)) == 0  # already held
+        captured.clear()
+        while sched.has_work:
+            sched.step()
+    ops.check_device_errors(cuda)
+    assert captured == [], f"decode steps captured graphs mid-run: {captured}"
+    assert [r.sequence[0].tolist() for r in reqs] == eager_tokens
+
+
 @pytest.mark.parametrize("chunk", [32, None])
 def test_cuda_graph_decode_matches_eager(cuda, chunk):
     """Decode steps replayed from CUDA graphs give the eager path's tokens and logits."""
