@@ -291,7 +291,7 @@ class PDRank:
             prompts, h2d = self.resident, 0
         if self.prefill:
             run_prefill(self.model, self.cache, self.channel, [(i, prompts[i]) for i in mine],
-                        token_budget=4096, idle_sleep=0.0002, clock=clock,
+                        token_budget=4096, chunk_size=2048, idle_sleep=0.0002, clock=clock,
                         arrival=None if arrival is None else [arrival[i] for i in mine], first_token_at=record)
             return h2d, 0, None
         reqs = run_decode(self.model, self.cache, self.channel, prompts.__getitem__,
@@ -396,7 +396,7 @@ def run_pd(args, dist_ctx, rank, local, device, world):
             "config": {
                 "workload": f"config5 P/D, closed loop: Llama-3.2-1B shape, the same {len(base)} requests per pair "
                             f"(prompts log-normal mean 1024 capped 8192, per pair sum {sum(lens)}, max {max(lens)}), "
-                            f"{args.new_tokens} greedy new tokens; prefill batches <=4096 tokens; KV blocks pulled "
+                            f"{args.new_tokens} greedy new tokens; prefill batches <=4096 tokens in chunks <=2048; KV blocks pulled "
                             "over NVLink by the decode GPU",
                 "global_batch": len(host),
                 "parallelism": f"{world // 2} P/D pairs (prefill rank 2k, decode rank 2k+1) behind the router",

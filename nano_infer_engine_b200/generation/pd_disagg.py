@@ -315,6 +315,7 @@ def run_prefill(
     requests: list[tuple[int, torch.Tensor]],
     *,
     token_budget: int = 8192,
+    chunk_size: int | None = None,
     arrival: list[float] | None = None,
     clock: Callable[[], float] = time.perf_counter,
     idle_sleep: float = 0.0,
@@ -324,57 +325,92 @@ def run_prefill(
 
     Batches are formed from arrived requests up to ``token_budget`` prompt
     tokens and the free blocks of ``cache``; a request's blocks are held
-    until the decode peer acknowledges its copy.  ``arrival`` (``clock()``
-    times, same order as ``requests``) gates admission for open-loop runs;
+    until the decode peer acknowledges its copy.  With ``chunk_size`` a
+    prompt is prefilled in chunks of at most that many tokens: each batch
+    first continues the requests already started (oldest first), then starts
+    arrived ones, the last chunk of a batch cut to fit the budget, so a long
+    prompt shares its batches with the prompts behind it; a request is handed
+    off after its last chunk (the reference prefills each prompt whole,
+    generation/pd_scheduler.py:136-145).  Without it every prompt is one
+    chunk and a batch never splits one.  ``arrival`` (``clock()`` times, same
+    order as ``requests``) gates admission for open-loop runs;
     ``first_token_at`` receives, per request index, the ``clock()`` time at
     which its first token was known, so TTFT = first_token_at - arrival on one
     time base.
     """
+    if chunk_size is not None and chunk_size <= 0:
+        raise ValueError("chunk_size must be positive")
     stats = PrefillStats()
     pending = deque(range(len(requests)))
+    started: deque[int] = deque()  # chunked requests with prompt tokens still to prefill
+    done: dict[int, int] = {}  # prompt tokens already in the cache, per started request
     held: dict[int, str] = {}
     bs = cache.block_size
-    while pending or held:
+    while pending or started or held:
         for msg in channel.poll():
             if msg[0] == ACK:
                 cache.release(held.pop(msg[1]))
-        batch: list[int] = []
+        batch: list[tuple[int, int, int]] = []  # (request, first token, end token) of each chunk
         tokens = 0
-        blocks = 0
+        # blocks not yet allocated and not promised to a started request: a
+        # request starts only when its whole prompt fits, so started requests
+        # always finish (their blocks are freed on the peer's ACK)
+        free = cache.allocator.free_block_count
+        free -= sum(-(-requests[k][1].shape[1] // bs) - (-(-done[k] // bs)) for k in started)
+        for k in started:
+            n, at = requests[k][1].shape[1], done[k]
+            take = min(n - at, chunk_size, token_budget - tokens)
+            if take <= 0:
+                break
+            batch.append((k, at, at + take))
+            tokens += take
         now = clock()
-        while pending:
+        while pending and len(batch) == len(started) and tokens < token_budget:
             k = pending[0]
             if arrival is not None and arrival[k] > now:
                 break
             n = requests[k][1].shape[1]
+            take = n if chunk_size is None else min(n, chunk_size, token_budget - tokens)
+            if chunk_size is None and batch and tokens + n > token_budget:
+                break
             need = -(-n // bs)
-            if batch and (tokens + n > token_budget or blocks + need > cache.allocator.free_block_count):
+            if need > free:
                 break
-            if not batch and need > cache.allocator.free_block_count:
-                break
-            batch.append(pending.popleft())
-            tokens += n
-            blocks += need
+            batch.append((pending.popleft(), 0, take))
+            tokens += take
+            free -= need
         if not batch:
             if idle_sleep:
                 time.sleep(idle_sleep)
             continue
-        ids = tuple(f"pd-{requests[k][0]}" for k in batch)
-        chunks = tuple(requests[k][1] for k in batch)
+        ids = tuple(f"pd-{requests[k][0]}" for k, _, _ in batch)
+        chunks = tuple(requests[k][1][:, a:e] for k, a, e in batch)
         with torch.inference_mode():
             logits = paged_prefill_chunks(model, chunks, cache, ids)
             picked = ops.argmax_rows(logits) if logits.is_cuda else logits.argmax(dim=-1)
             first = picked.tolist()  # also waits for the KV writes
-        if first_token_at is not None:
+        finished = []
+        for (k, a, e), tok in zip(batch, first):
+            if e < requests[k][1].shape[1]:
+                if a == 0:
+                    started.append(k)
+                done[k] = e
+                continue
+            if a > 0:
+                started.remove(k)
+                del done[k]
+            finished.append((k, tok))
+        if first_token_at is not None and finished:
             now = clock()
-            for k in batch:
+            for k, _ in finished:
                 first_token_at[requests[k][0]] = now
-        for k, sid, tok in zip(batch, ids, first):
+        for k, tok in finished:
             index, prompt = requests[k]
+            sid = f"pd-{index}"
             table = cache.get_block_table(sid)
             channel.send([HANDOFF, index, prompt.shape[1], int(tok), len(table), 0, 0, 0, *table])
             held[index] = sid
-        stats.requests += len(batch)
+            stats.requests += 1
         stats.tokens += tokens
         stats.batches += 1
     channel.send([DONE, stats.requests])

@@ -17,6 +17,9 @@ import torch.multiprocessing as mp
 
 from nano_infer_engine_b200.generation.config import GenerationConfig
 from nano_infer_engine_b200.generation.pd_disagg import (
+    ACK,
+    DONE,
+    HANDOFF,
     HEADER_WORDS,
     PairChannel,
     PipeChannel,
@@ -222,3 +225,84 @@ def test_two_pairs_split_requests_over_four_ranks(tmp_path):
         assert dec["done"] == sorted(pre["mine"])
         assert dec["status"] == ["completed"]
         assert pre["free"] == 16 and dec["free"] == 64
+
+
+class _LoopbackChannel:
+    """In-process stand-in for the pair channel: every hand-off is acknowledged at the next poll."""
+
+    def __init__(self):
+        self.sent = []
+        self._acks = []
+
+    def send(self, words):
+        self.sent.append(list(words))
+        if words[0] == HANDOFF:
+            self._acks.append([ACK, words[1]])
+
+    def poll(self, stop_after=None):
+        acks, self._acks = self._acks, []
+        return acks
+
+    def close(self):
+        pass
+
+
+def test_chunked_prefill_plan_budget_order_and_handoffs():
+    from test_scheduler_host import ScriptedModel
+
+    prompts = _prompts()
+    model = ScriptedModel({f"pd-{i}": tuple(range(1, 20)) for i in range(len(prompts))})
+    cache = PagedKVCache(64, 4, 1, 1, 4, torch.float32, "cpu")
+    channel = _LoopbackChannel()
+    stats = run_prefill(model, cache, channel, list(enumerate(prompts)), token_budget=12, chunk_size=8)
+    spans = {}  # sequence -> list of chunk lengths, in call order
+    for sids, bounds in model.ragged_calls:
+        assert bounds[-1] <= 12  # the token budget holds for every batch
+        lengths = [b - a for a, b in zip(bounds, bounds[1:])]
+        assert all(0 < n <= 8 for n in lengths)
+        for sid, n in zip(sids, lengths):
+            spans.setdefault(sid, []).append(n)
+    for i, p in enumerate(prompts):
+        assert sum(spans[f"pd-{i}"]) == p.shape[1]  # every prompt token prefilled exactly once
+    # requests start in arrival order, and a started request is continued in
+    # every batch (ahead of new ones) until its last chunk
+    firsts = []
+    for sids, _ in model.ragged_calls:
+        firsts.extend(s for s in sids if s not in firsts)
+    assert firsts == [f"pd-{i}" for i in range(len(prompts))]
+    left = {f"pd-{i}": p.shape[1] for i, p in enumerate(prompts)}
+    for sids, bounds in model.ragged_calls:
+        unfinished_before = [s for s in firsts[: firsts.index(sids[-1]) + 1] if 0 < left[s] < prompts[int(s[3:])].shape[1]]
+        assert list(sids[: len(unfinished_before)]) == unfinished_before
+        for sid, a_, b_ in zip(sids, bounds, bounds[1:]):
+            left[sid] -= b_ - a_
+    handoffs = [m for m in channel.sent if m[0] == HANDOFF]
+    assert sorted(m[1] for m in handoffs) == list(range(len(prompts)))
+    for m in handoffs:
+        index, length, token, nblk = m[1], m[2], m[3], m[4]
+        assert length == prompts[index].shape[1] and nblk == -(-length // 4)
+        assert token == len(spans[f"pd-{index}"])  # the scripted token of the request's last chunk
+    assert channel.sent[-1][0] == DONE and stats.requests == len(prompts)
+    assert stats.tokens == sum(p.shape[1] for p in prompts)
+    assert cache.allocator.free_block_count == 64  # every hand-off acknowledged and freed
+
+
+def test_chunked_prefill_starts_a_request_only_when_its_whole_prompt_fits():
+    from test_scheduler_host import ScriptedModel
+
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, 8, (1, n), generator=g) for n in (40, 40, 6)]
+    model = ScriptedModel()
+    cache = PagedKVCache(12, 4, 1, 1, 4, torch.float32, "cpu")  # 48 tokens: one 40-token prompt at a time
+    channel = _LoopbackChannel()
+    stats = run_prefill(model, cache, channel, list(enumerate(prompts)), token_budget=16, chunk_size=8)
+    assert stats.requests == 3 and cache.allocator.free_block_count == 12
+    # request 1 may not start before request 0 is handed off and its blocks are back
+    first_call_of_1 = next(n for n, (sids, _) in enumerate(model.ragged_calls) if "pd-1" in sids)
+    last_call_of_0 = max(n for n, (sids, _) in enumerate(model.ragged_calls) if "pd-0" in sids)
+    assert first_call_of_1 > last_call_of_0
+
+
+def test_chunk_size_must_be_positive():
+    with pytest.raises(ValueError, match="chunk_size"):
+        run_prefill(None, PagedKVCache(4, 4, 1, 1, 4, torch.float32, "cpu"), _LoopbackChannel(), [], chunk_size=0)

@@ -233,3 +233,63 @@ def test_pd_greedy_checks_before_any_work(cuda):
                            prefill_cache, decode_cache)
     assert prefill_cache.allocator.allocated_block_count == 0
     assert decode_cache.allocator.allocated_block_count == 0
+
+
+def _all_layers(cache, sid, length):
+    pairs = [cache.gather(layer, sid, length) for layer in range(cache.num_layers)]
+    return torch.stack([k for k, _ in pairs]), torch.stack([v for _, v in pairs])
+
+
+class _LoopbackChannel:
+    """In-process pair channel: each hand-off is acknowledged at the next poll,
+    after the request's KV is copied out of the prefill pool."""
+
+    def __init__(self, cache):
+        self.cache = cache
+        self.handoffs = {}
+        self._acks = []
+
+    def send(self, words):
+        from nano_infer_engine_b200.generation.pd_disagg import ACK, HANDOFF
+
+        if words[0] == HANDOFF:
+            sid = f"pd-{words[1]}"
+            self.handoffs[sid] = (words[3], words[2], *_all_layers(self.cache, sid, words[2]))
+            self._acks.append([ACK, words[1]])
+
+    def poll(self, stop_after=None):
+        acks, self._acks = self._acks, []
+        return acks
+
+    def close(self):
+        pass
+
+
+@pytest.mark.parametrize("chunk_size,budget", [(16, 40), (1, 8), (64, 64)])
+def test_chunked_pd_prefill_matches_reference_first_tokens_and_whole_prompt_kv(cuda, chunk_size, budget):
+    """run_prefill with chunking: the first token of every request is the reference's (golden), and
+    the KV handed off equals a whole-prompt prefill of the same prompt."""
+    from nano_infer_engine_b200 import ops
+    from nano_infer_engine_b200.generation.paged_prefill import paged_prefill
+    from nano_infer_engine_b200.generation.pd_disagg import run_prefill
+
+    model = _model(cuda)
+    prompts = [p.to(cuda) for p in recipes.pd_prompts()]
+    cache = _cache(cuda, recipes.PD_PREFILL_BLOCKS)
+    channel = _LoopbackChannel(cache)
+    stats = run_prefill(model, cache, channel, list(enumerate(prompts)), token_budget=budget, chunk_size=chunk_size)
+    ops.check_device_errors(cuda)
+    assert stats.requests == len(prompts) and stats.tokens == sum(p.shape[1] for p in prompts)
+    assert cache.allocator.free_block_count == recipes.PD_PREFILL_BLOCKS
+    whole = _cache(cuda, recipes.PD_PREFILL_BLOCKS)
+    for i, prompt in enumerate(prompts):
+        sid = f"pd-{i}"
+        token, length, k, v = channel.handoffs[sid]
+        assert length == prompt.shape[1]
+        assert token == GOLDEN["scheduler"]["tokens"][sid][0], sid
+        with torch.inference_mode():
+            paged_prefill(model, (prompt,), whole, (sid,))
+        wk, wv = _all_layers(whole, sid, length)
+        torch.testing.assert_close(k, wk, atol=1e-4, rtol=0)
+        torch.testing.assert_close(v, wv, atol=1e-4, rtol=0)
+        whole.release(sid)
