@@ -22,6 +22,40 @@ from ..models.llama import HOST_BOUNDARIES, LAST_ROWS_DONE, LAST_ROWS_ONLY
 from ..paged_cache import PagedKVCache
 
 
+def _flat_view(chunks: tuple[torch.Tensor, ...]) -> torch.Tensor | None:
+    """The chunks as one 1-D tensor without a copy when they are consecutive
+    pieces of one buffer (a decode step's sampled tokens), else None."""
+    first = chunks[0]
+    if first.stride(1) != 1:
+        return None
+    p = first.data_ptr()
+    storage = first.untyped_storage().data_ptr()
+    size = first.element_size()
+    total = 0
+    for c in chunks:
+        if c.dtype != first.dtype or c.data_ptr() != p + total * size or c.untyped_storage().data_ptr() != storage:
+            return None
+        if c.shape[1] > 1 and c.stride(1) != 1:
+            return None
+        total += c.shape[1]
+    return first.as_strided((total,), (1,))
+
+
+_ONE_TOKEN_QSL: dict[tuple[torch.device, int], torch.Tensor] = {}
+
+
+def _one_token_boundaries(device: torch.device, n: int) -> torch.Tensor:
+    """query_start_loc of n one-token chunks (0 .. n), uploaded once per device
+    and size; callers only read it."""
+    qsl = _ONE_TOKEN_QSL.get((device, n))
+    if qsl is None:
+        qsl = torch.arange(n + 1, dtype=torch.long).to(device)
+        setattr(qsl, HOST_BOUNDARIES, list(range(n + 1)))
+        setattr(qsl, LAST_ROWS_ONLY, True)
+        _ONE_TOKEN_QSL[(device, n)] = qsl
+    return qsl
+
+
 def _validate_paged_prefill_inputs(
     prompts: tuple[torch.Tensor, ...],
     paged_cache: PagedKVCache,
@@ -119,15 +153,20 @@ def paged_prefill_chunks(
     if len(set(sequence_ids)) != len(sequence_ids):
         raise ValueError("sequence IDs must be unique")
 
-    flat = torch.cat([c[0] for c in chunks])
-    boundaries = [0]
-    for c in chunks:
-        boundaries.append(boundaries[-1] + c.shape[1])
-    query_start_loc = torch.tensor(boundaries, dtype=torch.long)
-    if flat.is_cuda:
-        query_start_loc = query_start_loc.pin_memory().to(flat.device, non_blocking=True)
-    setattr(query_start_loc, HOST_BOUNDARIES, boundaries)
-    setattr(query_start_loc, LAST_ROWS_ONLY, True)
+    flat = _flat_view(chunks)
+    if flat is None:
+        flat = torch.cat([c[0] for c in chunks])
+    if flat.is_cuda and flat.numel() == len(chunks):
+        query_start_loc = _one_token_boundaries(flat.device, len(chunks))  # a decode-only step
+    else:
+        boundaries = [0]
+        for c in chunks:
+            boundaries.append(boundaries[-1] + c.shape[1])
+        query_start_loc = torch.tensor(boundaries, dtype=torch.long)
+        if flat.is_cuda:
+            query_start_loc = query_start_loc.pin_memory().to(flat.device, non_blocking=True)
+        setattr(query_start_loc, HOST_BOUNDARIES, boundaries)
+        setattr(query_start_loc, LAST_ROWS_ONLY, True)
     try:
         forward_ragged = model.forward_ragged
     except AttributeError:

@@ -29,6 +29,23 @@ from .paged_prefill import _validate_paged_prefill_inputs, paged_prefill, paged_
 from .request import PagedRequest, RequestStatus
 
 
+def _rows_view(rows: list[torch.Tensor]) -> torch.Tensor | None:
+    """``rows`` as one [len, V] tensor without a copy when they are consecutive
+    rows of one buffer (the decode batch's logits), else None."""
+    first = rows[0]
+    if first.ndim != 1 or first.stride(0) != 1:
+        return None
+    n = first.shape[0]
+    step = n * first.element_size()
+    p0 = first.data_ptr()
+    storage = first.untyped_storage().data_ptr()
+    for i, r in enumerate(rows):
+        if (r.ndim != 1 or r.shape[0] != n or r.dtype != first.dtype or r.stride(0) != 1
+                or r.data_ptr() != p0 + i * step or r.untyped_storage().data_ptr() != storage):
+            return None
+    return first.as_strided((len(rows), n), (n, 1))
+
+
 class _PendingTokens:
     """Sampled token ids on their way to the host: a pinned buffer filled by an
     asynchronous copy, and the event that marks the copy's completion."""
@@ -322,7 +339,9 @@ class ContinuousBatchingScheduler:
         if not rows:
             empty = torch.empty((0, 1), dtype=torch.long, device=self.paged_cache.keys.device)
             return empty, []
-        stacked = torch.stack(rows)
+        stacked = _rows_view(rows)
+        if stacked is None:
+            stacked = torch.stack(rows)
         if stacked.is_cuda and stacked.ndim == 2 and len(rows) <= ops.ARGMAX_MAX_ROWS:
             next_tokens = ops.argmax_rows(stacked).unsqueeze(-1)  # one launch, torch.argmax's answer
         else:

@@ -258,3 +258,28 @@ def test_deferred_token_read_keeps_plans_tokens_and_events(chunk, monkeypatch):
     sync = run(False)
     deferred = run(True)
     assert deferred == sync
+
+
+def test_sampler_reads_consecutive_logits_rows_without_a_copy():
+    from nano_infer_engine_b200.generation.scheduler import _rows_view
+
+    logits = torch.randn(5, 7)
+    view = _rows_view([logits[i] for i in range(5)])
+    assert view is not None and view.data_ptr() == logits.data_ptr() and torch.equal(view, logits)
+    assert torch.equal(_rows_view([logits[i] for i in range(1, 4)]), logits[1:4])
+    assert _rows_view([logits[0], logits[2]]) is None  # a gap
+    assert _rows_view([logits[1], logits[0]]) is None  # out of order
+    assert _rows_view([logits[0], torch.randn(7)]) is None  # another buffer
+
+
+def test_prefill_chunks_that_tile_one_buffer_are_passed_without_a_copy():
+    from nano_infer_engine_b200.generation.paged_prefill import _flat_view
+
+    tokens = torch.arange(10).view(10, 1)  # a decode step's sampled tokens
+    view = _flat_view(tuple(tokens[i : i + 1] for i in range(10)))
+    assert view is not None and view.data_ptr() == tokens.data_ptr() and torch.equal(view, torch.arange(10))
+    prompt = torch.arange(20).view(1, 20)
+    assert torch.equal(_flat_view((prompt[:, 0:5], prompt[:, 5:12], prompt[:, 12:20])), torch.arange(20))
+    assert _flat_view((prompt[:, 0:5], prompt[:, 6:12])) is None  # a gap
+    assert _flat_view((prompt[:, 5:8], prompt[:, 0:5])) is None  # out of order
+    assert _flat_view((tokens[0:1], torch.zeros(1, 1, dtype=torch.long))) is None  # another buffer
