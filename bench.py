@@ -318,7 +318,7 @@ def time_pd(pd, steps, warmup, dist_ctx, e2e=False):
 
     with torch.inference_mode():
         for _ in range(warmup):
-            pd.step()
+            pd.step(e2e)
         torch.cuda.synchronize()
         barrier(dist_ctx)
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -359,7 +359,7 @@ def run_pd(args, dist_ctx, rank, local, device, world):
     e2e = None
     if not args.no_e2e:
         e2e_steps = max(2, args.steps)
-        e2e_s, (_, h2d, d2h) = time_pd(pd, e2e_steps, 0, dist_ctx, e2e=True)
+        e2e_s, (_, h2d, d2h) = time_pd(pd, e2e_steps, 1, dist_ctx, e2e=True)
         e2e = {"value": len(host) * args.new_tokens * e2e_steps / e2e_s, "unit": UNIT,
                "h2d_bytes_per_step": h2d // e2e_steps, "d2h_bytes_per_step": d2h // e2e_steps}
     pd.close()
