@@ -76,6 +76,8 @@ def parse_args():
                         "(Poisson arrivals, TTFT/TPOT, transfer GB/s; even N >= 2)")
     p.add_argument("--pd-requests", type=int, default=512)
     p.add_argument("--pd-rate", type=float, default=20.0)
+    p.add_argument("--pd-decode-per-prefill", type=int, default=1,
+                   help="N >= 2: decode ranks fed by each prefill rank (1 = prefill/decode pairs)")
     p.add_argument("--decode-batch", type=int, default=64)
     p.add_argument("--decode-blocks", type=int, default=131072)
     return p.parse_args()
@@ -228,46 +230,56 @@ def pd_workload(num_requests, seed=SEED):
 
 
 class PDRank:
-    """One rank of a prefill/decode pair: even ranks prefill, odd ranks decode.
+    """One rank of a P/D group: rank g*j prefills for the decode ranks
+    g*j+1 .. g*j+k of its group (g = k + 1; k = 1 is a pair).
 
-    The router (``assign_pairs``, least outstanding prompt+output tokens)
-    splits the job's requests over the pairs identically on every rank; the
-    prefill rank's KV pool is mapped into its decode peer with CUDA IPC and
-    blocks are pulled with the block-copy kernel.
+    The router (``assign_groups``, least outstanding prompt+output tokens)
+    splits the job's requests over the groups and, inside a group, over its
+    decode ranks, identically on every rank; the prefill rank's KV pool is
+    mapped into each of its decode ranks with CUDA IPC and blocks are pulled
+    with the block-copy kernel.
     """
 
-    def __init__(self, dist_ctx, rank, world, device, model, host_prompts, new_tokens):
+    def __init__(self, dist_ctx, rank, world, device, model, host_prompts, new_tokens, decode_per_prefill=1):
         from nano_infer_engine_b200.generation.pd_disagg import (
             HEADER_WORDS,
             PipeChannel,
-            assign_pairs,
+            assign_groups,
             gpu_import,
             open_peer_pool,
             publish_pool,
         )
         from nano_infer_engine_b200.paged_cache import PagedKVCache
 
+        k = decode_per_prefill
+        g = k + 1
         self.device = device
         self.model = model
         self.new_tokens = new_tokens
-        self.prefill = rank % 2 == 0
+        self.prefill = rank % g == 0
         self.rank = rank
-        self.peer = rank ^ 1
+        head = rank - rank % g
+        self.peers = [head + 1 + j for j in range(k)] if self.prefill else [head]
         self.store = dist_ctx.distributed_c10d._get_default_store()
         work = [p.shape[1] + new_tokens for p in host_prompts]
-        self.mine = assign_pairs(work, world // 2)[rank // 2]
+        slots = assign_groups(work, world // g, k)[rank // g]
+        if self.prefill:
+            self.route = {i: j for j, slot in enumerate(slots) for i in slot}
+            self.mine = sorted(self.route)
+        else:
+            self.mine = slots[rank % g - 1]
         self.host = {i: host_prompts[i] for i in self.mine}
         self.resident = {i: p.to(device) for i, p in self.host.items()}
         longest = max(p.shape[1] for p in host_prompts)
-        # the two ranks of a pair share a node: records go over a pair of named pipes
-        self.channel = PipeChannel(self.store, rank, self.peer, HEADER_WORDS + -(-longest // 16))
+        # the ranks of a group share a node: records go over pairs of named pipes
+        self.channels = [PipeChannel(self.store, rank, peer, HEADER_WORDS + -(-longest // 16)) for peer in self.peers]
         blocks = sum(-(-(self.host[i].shape[1] + (0 if self.prefill else new_tokens)) // 16) for i in self.mine)
         self.cache = PagedKVCache(blocks + 64, 16, 16, 8, 64, torch.bfloat16, device)
         if self.prefill:
             publish_pool(self.store, rank, self.cache)
             self.remote = None
         else:
-            self.remote = open_peer_pool(self.store, self.peer, self.cache)
+            self.remote = open_peer_pool(self.store, self.peers[0], self.cache)
             self.transfers = []
             self.pull = gpu_import(self.remote, self.transfers)
             # decode graphs for batch sizes up to graph_batches are captured during
@@ -290,11 +302,12 @@ class PDRank:
         else:
             prompts, h2d = self.resident, 0
         if self.prefill:
-            run_prefill(self.model, self.cache, self.channel, [(i, prompts[i]) for i in mine],
-                        token_budget=4096, chunk_size=2048, idle_sleep=0.0002, clock=clock,
-                        arrival=None if arrival is None else [arrival[i] for i in mine], first_token_at=record)
+            run_prefill(self.model, self.cache, self.channels, [(i, prompts[i]) for i in mine],
+                        token_budget=4096, chunk_size=2048, route=[self.route[i] for i in mine], idle_sleep=0.0002,
+                        clock=clock, arrival=None if arrival is None else [arrival[i] for i in mine],
+                        first_token_at=record)
             return h2d, 0, None
-        reqs = run_decode(self.model, self.cache, self.channel, prompts.__getitem__,
+        reqs = run_decode(self.model, self.cache, self.channels[0], prompts.__getitem__,
                           GenerationConfig(max_new_tokens=self.new_tokens), len(mine), self.pull,
                           self.model.config.vocab_size, idle_sleep=0.0002, clock=clock, timings=record,
                           graph_batches=self.graph_batches)
@@ -309,8 +322,10 @@ class PDRank:
         if self.remote is not None:
             close_peer_pool(self.store, self.rank, self.remote)
         else:
-            wait_pool_unmapped(self.store, self.peer)
-        self.channel.release()
+            for peer in self.peers:
+                wait_pool_unmapped(self.store, peer)
+        for channel in self.channels:
+            channel.release()
 
 
 def time_pd(pd, steps, warmup, dist_ctx, e2e=False):
@@ -335,24 +350,29 @@ def time_pd(pd, steps, warmup, dist_ctx, e2e=False):
     return max_over_ranks(dist_ctx, elapsed, pd.device), [int(x) for x in totals.tolist()]
 
 
-def pd_job(pairs, new_tokens):
-    """The closed-loop job for `pairs` P/D pairs: the same seeded 32-request set
-    (config 5's prompt-length distribution) for every pair, interleaved one copy
-    per pair per request.  The least-outstanding-work router then hands every
-    pair one copy of each request, so the per-pair workload is identical at
-    every N (weak scaling on a fixed per-pair job)."""
+def pd_job(decode_ranks, new_tokens):
+    """The closed-loop job for ``decode_ranks`` decode GPUs: the same seeded
+    32-request set (config 5's prompt-length distribution) for every decode
+    rank, interleaved one copy per decode rank per request.  The
+    least-outstanding-work router then hands every decode rank one copy of
+    each request, so the per-decode-rank workload is identical at every N and
+    P:D ratio (weak scaling on a fixed job per decode GPU)."""
     base = pd_workload(2 * PD_REQUESTS_PER_GPU)
-    job = [p for p in base for _ in range(pairs)]
+    job = [p for p in base for _ in range(decode_ranks)]
     return base, job
 
 
 def run_pd(args, dist_ctx, rank, local, device, world):
-    """N >= 2 (even): N/2 prefill/decode pairs behind the router, weak scaling
-    (the same 32-request set per pair), closed loop: one step = every pair generates its batch."""
+    """N >= 2: N/(k+1) groups of one prefill rank and k decode ranks behind the
+    router (k = --pd-decode-per-prefill; 1 = pairs), weak scaling (the same
+    32-request set per decode rank), closed loop: one step = every decode rank
+    generates its batch."""
+    k = args.pd_decode_per_prefill
+    groups = world // (k + 1)
     model = build_engine(device)
-    base, job = pd_job(world // 2, args.new_tokens)
+    base, job = pd_job(groups * k, args.new_tokens)
     host = [p.pin_memory() for p in job]
-    pd = PDRank(dist_ctx, rank, world, device, model, host, args.new_tokens)
+    pd = PDRank(dist_ctx, rank, world, device, model, host, args.new_tokens, k)
     with ClockSampler(local) as clocks:
         elapsed, (launches, _, _) = time_pd(pd, args.steps, args.warmup, dist_ctx)
     value = len(host) * args.new_tokens * args.steps / elapsed
@@ -381,7 +401,8 @@ def run_pd(args, dist_ctx, rank, local, device, world):
         print(json.dumps({
             "metric": METRIC,
             "value": value,
-            "per_pair": value / (world // 2),
+            "per_group": value / groups,
+            "per_decode_gpu": value / (groups * k),
             "per_gpu": value / world,
             "unit": UNIT,
             "n_gpus": world,
@@ -394,12 +415,12 @@ def run_pd(args, dist_ctx, rank, local, device, world):
             "dtype": "bf16",
             "data": "synthetic (seeded prompts, random-init weights N(0, 0.02))",
             "config": {
-                "workload": f"config5 P/D, closed loop: Llama-3.2-1B shape, the same {len(base)} requests per pair "
-                            f"(prompts log-normal mean 1024 capped 8192, per pair sum {sum(lens)}, max {max(lens)}), "
+                "workload": f"config5 P/D, closed loop: Llama-3.2-1B shape, the same {len(base)} requests per decode GPU "
+                            f"(prompts log-normal mean 1024 capped 8192, per decode GPU sum {sum(lens)}, max {max(lens)}), "
                             f"{args.new_tokens} greedy new tokens; prefill batches <=4096 tokens in chunks <=2048; KV blocks pulled "
                             "over NVLink by the decode GPU",
                 "global_batch": len(host),
-                "parallelism": f"{world // 2} P/D pairs (prefill rank 2k, decode rank 2k+1) behind the router",
+                "parallelism": f"{groups} P/D groups of 1 prefill + {k} decode ranks behind the router",
                 "l2": "inputs larger than L2 (2.47 GB of weights streamed per decode step)",
             },
             "roofline": roofline,
@@ -427,11 +448,12 @@ def _pct(values, q):
 
 
 def run_pd_open(args, dist_ctx, rank, local, device, world):
-    """Config 5 open loop on N/2 pairs: output tok/s (arrival-capped), TTFT, TPOT, transfer GB/s."""
+    """Config 5 open loop on N/(k+1) P/D groups: output tok/s (arrival-capped), TTFT, TPOT, transfer GB/s."""
+    k = args.pd_decode_per_prefill
     model = build_engine(device)
     host, arrival = pd_open_workload(args.pd_requests, args.pd_rate)
     host = [p.pin_memory() for p in host]
-    pd = PDRank(dist_ctx, rank, world, device, model, host, args.new_tokens)
+    pd = PDRank(dist_ctx, rank, world, device, model, host, args.new_tokens, k)
     with torch.inference_mode():
         pd.step(indices=pd.mine[:16])  # warm-up: graphs, workspaces, allocator
         if not pd.prefill:
@@ -462,7 +484,7 @@ def run_pd_open(args, dist_ctx, rank, local, device, world):
         ttft, tpot, moved = [], [], []
         for r in range(world):
             data = json.loads(store.get(f"pdopen/{r}"))
-            if r % 2 == 0:
+            if r % (k + 1) == 0:
                 ttft.extend(data.values())
             else:
                 tpot.extend(data["tpot"].values())
@@ -471,7 +493,8 @@ def run_pd_open(args, dist_ctx, rank, local, device, world):
         print(json.dumps({
             "mode": "pd-open (config 5)",
             "n_gpus": world,
-            "pairs": world // 2,
+            "groups": world // (k + 1),
+            "decode_per_prefill": k,
             "requests": args.pd_requests,
             "rate_req_s": args.pd_rate,
             "new_tokens": args.new_tokens,
@@ -906,11 +929,14 @@ def main():
         __graft_entry__.build()
     barrier(dist_ctx)
     world = dist_ctx.get_world_size() if dist_ctx else 1
-    if world >= 2 and world % 2 == 0 and args.only == "pd-open":
+    group = args.pd_decode_per_prefill + 1
+    if args.pd_decode_per_prefill < 1:
+        raise SystemExit("--pd-decode-per-prefill must be >= 1")
+    if world >= 2 and world % group == 0 and args.only == "pd-open":
         return run_pd_open(args, dist_ctx, rank, local, device, world)
     if args.only == "pd-open":
-        raise SystemExit("--only pd-open needs an even number of GPUs >= 2 under torchrun")
-    if world >= 2 and world % 2 == 0 and args.only in ("all", "engine"):
+        raise SystemExit("--only pd-open needs a multiple of (--pd-decode-per-prefill + 1) GPUs >= 2 under torchrun")
+    if world >= 2 and world % group == 0 and args.only in ("all", "engine"):
         return run_pd(args, dist_ctx, rank, local, device, world)
     if args.only == "decode":
         dec = decode_config3(device, args.decode_iters, args.decode_batch, args.decode_blocks)

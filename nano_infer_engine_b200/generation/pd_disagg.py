@@ -47,6 +47,18 @@ DONE = 3
 HEADER_WORDS = 8
 
 
+def assign_groups(work: list[int], groups: int, decode_per_group: int) -> list[list[list[int]]]:
+    """Request indices per group and per decode rank of the group: the router
+    (``assign_pairs`` over the groups) picks the group, and inside it the same
+    least-outstanding-work rule picks the decode rank the prefill rank hands
+    the request to.  ``[group][decode slot] -> request indices``."""
+    out = []
+    for members in assign_pairs(work, groups):
+        slots = assign_pairs([work[i] for i in members], decode_per_group)
+        out.append([[members[j] for j in slot] for slot in slots])
+    return out
+
+
 def assign_pairs(work: list[int], num_pairs: int) -> list[list[int]]:
     """Request indices per pair: each request (in arrival order) goes to the pair
     with the least outstanding work so far (ties: lowest pair index)."""
@@ -311,11 +323,12 @@ class PrefillStats:
 def run_prefill(
     model,
     cache: PagedKVCache,
-    channel: PairChannel,
+    channel,
     requests: list[tuple[int, torch.Tensor]],
     *,
     token_budget: int = 8192,
     chunk_size: int | None = None,
+    route: list[int] | None = None,
     arrival: list[float] | None = None,
     clock: Callable[[], float] = time.perf_counter,
     idle_sleep: float = 0.0,
@@ -332,7 +345,10 @@ def run_prefill(
     prompt shares its batches with the prompts behind it; a request is handed
     off after its last chunk (the reference prefills each prompt whole,
     generation/pd_scheduler.py:136-145).  Without it every prompt is one
-    chunk and a batch never splits one.  ``arrival`` (``clock()`` times, same
+    chunk and a batch never splits one.  ``channel`` is the decode peer's
+    channel, or a list of channels when this rank feeds several decode ranks;
+    ``route[k]`` then names the channel of request k.  Acknowledgements are
+    taken from every channel and each one gets DONE.  ``arrival`` (``clock()`` times, same
     order as ``requests``) gates admission for open-loop runs;
     ``first_token_at`` receives, per request index, the ``clock()`` time at
     which its first token was known, so TTFT = first_token_at - arrival on one
@@ -340,6 +356,14 @@ def run_prefill(
     """
     if chunk_size is not None and chunk_size <= 0:
         raise ValueError("chunk_size must be positive")
+    channels = list(channel) if isinstance(channel, (list, tuple)) else [channel]
+    if route is None:
+        if len(channels) != 1:
+            raise ValueError("route is required with several channels")
+        route = [0] * len(requests)
+    if len(route) != len(requests) or any(not 0 <= c < len(channels) for c in route):
+        raise ValueError("route must name one channel per request")
+    sent = [0] * len(channels)
     stats = PrefillStats()
     pending = deque(range(len(requests)))
     started: deque[int] = deque()  # chunked requests with prompt tokens still to prefill
@@ -347,9 +371,10 @@ def run_prefill(
     held: dict[int, str] = {}
     bs = cache.block_size
     while pending or started or held:
-        for msg in channel.poll():
-            if msg[0] == ACK:
-                cache.release(held.pop(msg[1]))
+        for ch in channels:
+            for msg in ch.poll():
+                if msg[0] == ACK:
+                    cache.release(held.pop(msg[1]))
         batch: list[tuple[int, int, int]] = []  # (request, first token, end token) of each chunk
         tokens = 0
         # blocks not yet allocated and not promised to a started request: a
@@ -408,13 +433,15 @@ def run_prefill(
             index, prompt = requests[k]
             sid = f"pd-{index}"
             table = cache.get_block_table(sid)
-            channel.send([HANDOFF, index, prompt.shape[1], int(tok), len(table), 0, 0, 0, *table])
+            channels[route[k]].send([HANDOFF, index, prompt.shape[1], int(tok), len(table), 0, 0, 0, *table])
+            sent[route[k]] += 1
             held[index] = sid
             stats.requests += 1
         stats.tokens += tokens
         stats.batches += 1
-    channel.send([DONE, stats.requests])
-    channel.close()
+    for ch, n in zip(channels, sent):
+        ch.send([DONE, n])
+        ch.close()
     return stats
 
 

@@ -71,3 +71,21 @@ def test_oracle_weights_equal_the_engine_init():
         for name in want:
             assert state[name].dtype == want[name].dtype
             assert torch.equal(state[name], want[name]), name
+
+
+def test_pd_job_gives_every_decode_rank_the_same_requests():
+    """The closed-loop P/D job is weak scaling on a fixed job per decode GPU, for pairs and for
+    one prefill rank feeding several decode ranks."""
+    import bench
+    from nano_infer_engine_b200.generation.pd_disagg import assign_groups
+
+    base = None
+    for groups, k in ((1, 1), (2, 1), (4, 1), (1, 3), (2, 3)):
+        base, job = bench.pd_job(groups * k, 256)
+        want = sorted(p.shape[1] for p in base)
+        slots = assign_groups([p.shape[1] + 256 for p in job], groups, k)
+        assert len(slots) == groups and all(len(group) == k for group in slots)
+        for group in slots:
+            for slot in group:
+                assert sorted(job[i].shape[1] for i in slot) == want
+    assert sum(p.shape[1] for p in base) == 18376

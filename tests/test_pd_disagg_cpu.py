@@ -306,3 +306,68 @@ def test_chunked_prefill_starts_a_request_only_when_its_whole_prompt_fits():
 def test_chunk_size_must_be_positive():
     with pytest.raises(ValueError, match="chunk_size"):
         run_prefill(None, PagedKVCache(4, 4, 1, 1, 4, torch.float32, "cpu"), _LoopbackChannel(), [], chunk_size=0)
+
+
+def _group_worker(rank, port, result_path):
+    """One prefill rank (0) feeding two decode ranks (1, 2) over pipes: a 1:2 P:D group."""
+    from test_scheduler_host import ScriptedModel
+
+    from nano_infer_engine_b200.generation.pd_disagg import assign_groups
+
+    store = dist.TCPStore("127.0.0.1", port, 3, rank == 0, timeout=timedelta(seconds=60))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=3, timeout=timedelta(seconds=60))
+    prompts = _prompts()
+    work = [p.shape[1] + NEW_TOKENS for p in prompts]
+    (slots,) = assign_groups(work, 1, 2)
+    schedules = {f"pd-{i}": tuple(range(1, 8)) for i in range(len(prompts))}
+    words = HEADER_WORDS + 16
+    if rank == 0:
+        channels = [PipeChannel(store, 0, peer, words) for peer in (1, 2)]
+        mine = sorted(slots[0] + slots[1])
+        route = [0 if i in slots[0] else 1 for i in mine]
+        cache = PagedKVCache(16, 4, 1, 1, 4, torch.float32, "cpu")
+        stats = run_prefill(ScriptedModel(schedules), cache, channels, [(i, prompts[i]) for i in mine],
+                            token_budget=24, chunk_size=8, route=route, idle_sleep=0.001)
+        result = {"requests": stats.requests, "free": cache.allocator.free_block_count}
+    else:
+        channels = [PipeChannel(store, rank, 0, words)]
+        cache = PagedKVCache(64, 4, 1, 1, 4, torch.float32, "cpu")
+
+        def fake_import(c, sid, length, src_blocks):
+            c.ensure_capacity(sid, length)
+            c.advance(sid, length)
+            return None
+
+        reqs = run_decode(ScriptedModel(schedules), cache, channels[0], lambda i: prompts[i],
+                          GenerationConfig(max_new_tokens=NEW_TOKENS), 4, fake_import, 8, idle_sleep=0.001)
+        result = {"done": sorted(int(r.sequence_id[3:]) for r in reqs), "mine": sorted(slots[rank - 1]),
+                  "status": sorted({r.status.value for r in reqs}), "free": cache.allocator.free_block_count}
+    torch.save(result, f"{result_path}.{rank}")
+    dist.barrier()
+    for ch in channels:
+        ch.release()
+    dist.destroy_process_group()
+
+
+def test_one_prefill_rank_feeds_two_decode_ranks(tmp_path):
+    path = str(tmp_path / "grp")
+    mp.start_processes(_group_worker, args=(_free_port(), path), nprocs=3, start_method="spawn", join=True)
+    pre, d1, d2 = (torch.load(f"{path}.{r}") for r in range(3))
+    assert pre["requests"] == len(PROMPT_LENS) and pre["free"] == 16
+    assert d1["done"] == d1["mine"] and d2["done"] == d2["mine"]  # each decode rank got its routed requests
+    assert d1["mine"] and d2["mine"] and sorted(d1["mine"] + d2["mine"]) == list(range(len(PROMPT_LENS)))
+    assert d1["status"] == d2["status"] == ["completed"] and d1["free"] == d2["free"] == 64
+
+
+def test_group_router_gives_each_decode_rank_one_copy_of_a_replicated_job():
+    from nano_infer_engine_b200.generation.pd_disagg import assign_groups
+
+    base = [7, 30, 3, 12]
+    for groups, k in ((1, 3), (2, 3), (2, 1)):
+        copies = groups * k
+        job = [w for w in base for _ in range(copies)]  # copies of each request, interleaved
+        out = assign_groups(job, groups, k)
+        assert len(out) == groups and all(len(g) == k for g in out)
+        for group in out:
+            for slot in group:
+                assert sorted(job[i] for i in slot) == sorted(base)
