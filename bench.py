@@ -76,8 +76,9 @@ def parse_args():
                         "(Poisson arrivals, TTFT/TPOT, transfer GB/s; even N >= 2)")
     p.add_argument("--pd-requests", type=int, default=512)
     p.add_argument("--pd-rate", type=float, default=20.0)
-    p.add_argument("--pd-decode-per-prefill", type=int, default=1,
-                   help="N >= 2: decode ranks fed by each prefill rank (1 = prefill/decode pairs)")
+    p.add_argument("--pd-decode-per-prefill", type=int, default=None,
+                   help="N >= 2: decode ranks fed by each prefill rank (1 = prefill/decode pairs); default 3 when "
+                        "N is a multiple of 4 (one prefill GPU keeps three decode GPUs fed), else 1")
     p.add_argument("--decode-batch", type=int, default=64)
     p.add_argument("--decode-blocks", type=int, default=131072)
     return p.parse_args()
@@ -929,6 +930,8 @@ def main():
         __graft_entry__.build()
     barrier(dist_ctx)
     world = dist_ctx.get_world_size() if dist_ctx else 1
+    if args.pd_decode_per_prefill is None:
+        args.pd_decode_per_prefill = 3 if world % 4 == 0 else 1
     group = args.pd_decode_per_prefill + 1
     if args.pd_decode_per_prefill < 1:
         raise SystemExit("--pd-decode-per-prefill must be >= 1")
