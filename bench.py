@@ -16,11 +16,13 @@ prompts U[128, 2048], 256 greedy new tokens each, prefill chunk 128, at most
 * ``cpu_baseline`` - the CPU oracle (restated reference forward) on a bounded
                 sample of the same workload, extrapolated to tokens/s.
 
-N GPUs (torchrun), N even: N/2 prefill/decode pairs behind the router
-(BASELINE config 5's prompt-length distribution, 16 requests per GPU, closed
-loop, weak scaling, max-over-ranks time); the prefill GPU of a pair hands
-requests off and the decode GPU pulls their KV blocks over NVLink (CUDA IPC).
-Odd N: independent replicas of the 1-GPU run.
+N GPUs (torchrun), N a multiple of k + 1: N/(k+1) P/D groups of one prefill
+GPU feeding k decode GPUs behind the router (k = --pd-decode-per-prefill:
+by default 3 when N is a multiple of 4, else 1; BASELINE config 5's
+prompt-length distribution, the same 32 requests per decode GPU, closed
+loop, weak scaling, max-over-ranks time); the prefill GPU hands requests off
+and each decode GPU pulls their KV blocks over NVLink (CUDA IPC).  Other N:
+independent replicas of the 1-GPU run.
 ``--impl reference`` times the reference algorithm on the host cores (the
 oracle port; rank 0 only) for the same metric.
 """
@@ -73,7 +75,7 @@ def parse_args():
     p.add_argument("--only", choices=("all", "engine", "decode", "mixed", "pd-open", "linear"), default="all",
                    help="engine: headline run only; decode: config-3 decode micro-bench only; "
                         "mixed: config-4 mixed step only (profiling); pd-open: config 5 open loop "
-                        "(Poisson arrivals, TTFT/TPOT, transfer GB/s; even N >= 2)")
+                        "(Poisson arrivals, TTFT/TPOT, transfer GB/s; N >= 2, a multiple of k + 1)")
     p.add_argument("--pd-requests", type=int, default=512)
     p.add_argument("--pd-rate", type=float, default=20.0)
     p.add_argument("--pd-decode-per-prefill", type=int, default=None,
