@@ -623,7 +623,7 @@ def config4_decode(inp, out):
 def mixed_config4(device, iters):
     """8 prefill chunks of 128 at ctx U[0, 8192] + 120 decode rows at
     ctx U[256, 16384] (prefill first), one layer of the Llama-1B attention shape.
-    Times the tcgen05 varlen kernels (attention + split-KV combine) and the
+    Times the tcgen05 varlen kernel (attention, cut segments merged in-kernel) and the
     decode kernels separately, each as `iters` calls replayed from a CUDA graph."""
     from nano_infer_engine_b200 import ops
 
@@ -994,7 +994,7 @@ def main():
     mixed = mixed_config4(device, args.decode_iters)
     burst, _, tkind = measured_tensor_peaks()
     roofline_prefill = {"bound": "tensor", "achieved": mixed["prefill_tflops"], "peak": burst, "unit": "TFLOP/s",
-                        "frac": mixed["prefill_tflops"] / burst, "kernel": "prefill_tc_kernel + prefill_combine_kernel",
+                        "frac": mixed["prefill_tflops"] / burst, "kernel": "prefill_tc_kernel (cut segments merged in-kernel)",
                         "workload": f"config4 prefill rows: 8 x 128 queries at contexts {mixed['prefill_contexts']}, "
                                     f"{mixed['prefill_flops']} causal FLOPs/call",
                         "ms_per_launch": mixed["prefill_ms"], "peak_kind": f"{tkind} (bf16_tflops burst)",

@@ -10,11 +10,15 @@
 // one per CTA, with two CTAs per SM and one wave: every SM does the same
 // amount of work whatever the length mix (short segments cost more per tile),
 // and each CTA pays its prologue once.  A segment that lies wholly in one
-// CTA's range is normalised and written by that CTA; a segment cut by a range
-// boundary leaves (max, sum, unnormalised O) partials in one of two slots of
-// each CTA it touches, which prefill_combine_kernel (a dependent launch)
-// merges in CTA order.  Without a workspace each CTA takes exactly one
-// segment instead.
+// CTA's range is normalised and written by that CTA.  A segment cut by range
+// boundaries begins in the range of one CTA (its last segment, processed at
+// the end) and continues into the next ones (their first segment, processed
+// at their start): those later CTAs leave (max, sum, unnormalised O) partials
+// in the workspace and raise one flag per softmax warp, and the CTA where the
+// segment begins waits for the flags (bounded), merges in CTA order and
+// writes the rows.  All CTAs of the grid are resident at once (two per SM,
+// one wave), so the wait always ends.  Without a workspace each CTA takes
+// exactly one segment instead.
 //
 // Roles of the 6 warps of a CTA (all iterate the same segments / tiles):
 //   warp 4  TMA producer   per segment the Q tile (128 rows x 128 B) into one
@@ -59,6 +63,7 @@ constexpr int kPfStages = 4;
 constexpr int kPfThreads = 192;
 constexpr uint32_t kPfTmemCols = 256;
 constexpr uint32_t kPfWait = 1u << 22;
+constexpr uint32_t kPfMergeWait = 1u << 20;  // polls of a producer's flag (each an L2 round trip)
 constexpr int kPfTileQ = kPfBM * kPfHD * 2;       // 16 KiB
 constexpr int kPfTileKV = kPfBN * kPfHD * 2;      // 8 KiB
 constexpr int kPfBlockBytes = kPfBS * kPfHD * 2;  // 2 KiB
@@ -72,8 +77,8 @@ constexpr int kPfSegCost = 3;
 constexpr int kPfMaxUnits = 2048;  // 128-query tiles per call (larger calls use the generic kernel)
 constexpr int kPfMaxCtas = 320;    // persistent grid bound (2 per SM)
 constexpr int kPfPartialFloats = (2 + kPfHD) * kPfBM;  // m[128], l[128], O[64][128]
-// workspace: [cum: kPfMaxUnits + 2 int32 (cost prefix sums, then W) | partials]
-constexpr size_t kPfCumBytes = ((size_t)(kPfMaxUnits + 2) * sizeof(int32_t) + 255) & ~size_t(255);
+// workspace: [flags: kPfMaxCtas x 4 int32, zeroed by the host before each call | partials]
+constexpr size_t kPfFlagBytes = ((size_t)kPfMaxCtas * 4 * sizeof(int32_t) + 255) & ~size_t(255);
 
 struct PrefillArgs {
   __nv_bfloat16* out;
@@ -89,8 +94,8 @@ struct PrefillArgs {
   int tiles_per_req;
   int units;        // num_requests * tiles_per_req query tiles
   int stream;       // 1: equal tile ranges per CTA + partials; 0: one segment per CTA
-  float* partials;  // [grid][2] x kPfPartialFloats (stream mode)
-  int32_t* cum_out; // kPfCumBytes of the workspace (stream mode)
+  float* partials;  // [grid] x kPfPartialFloats (stream mode): a CTA's first segment when cut
+  int32_t* flags;   // [grid][4] (stream mode): softmax warp w of CTA c has written its rows of c's partial
   float scale;
   float scale_log2e;
   int scale_pow2;
@@ -123,6 +128,16 @@ __device__ __forceinline__ bool pf_wait(PfBars* b, uint64_t* bar, uint32_t parit
   *reinterpret_cast<volatile int*>(&b->abort) = 1;
   raise_flag(err, NIE_DEV_ERR_TIMEOUT);
   return false;
+}
+
+// Flag store / load with gpu-scope release / acquire ordering.
+__device__ __forceinline__ void st_release_gpu(int32_t* p, int32_t v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int32_t ld_acquire_gpu(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // The two halves of a bf16 pair as fp32 (exact).
@@ -288,10 +303,6 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     W = (total + gridDim.x - 1) / gridDim.x;
     lo = (int64_t)blockIdx.x * W;
     hi = min(total, lo + W);
-    if (blockIdx.x == 0) {
-      for (int u = threadIdx.x; u <= U; u += kPfThreads) a.cum_out[u] = b->cum[u];
-      if (threadIdx.x == 0) a.cum_out[kPfMaxUnits + 1] = (int32_t)W;
-    }
   } else {
     // one segment per CTA: blockIdx.x = unit * hq + head
     const int u = blockIdx.x / a.hq, h = blockIdx.x % a.hq;
@@ -299,7 +310,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     lo = (int64_t)a.hq * b->cum[u] + (int64_t)h * d;
     hi = lo + d;
   }
-  // the combine kernel may be staged now: it waits for this grid to complete
+  // a dependent launch after this kernel may be staged now (every CTA of this
+  // grid is resident once all have passed here)
   pdl_trigger();
   if (lo >= hi) return;  // uniform: nothing to do for this CTA
 
@@ -617,7 +629,10 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       tc_fence_before();
       mbar_arrive(&b->o_free[ob]);
       const bool whole = tlo == 0 && thi == seg.n;
-      if (t < x.nq && whole) {
+      // the three cases are uniform across the CTA (they depend on the
+      // segment and the range only), so whole warps take each branch
+      if (whole) {
+        if (t < x.nq) {
         const float inv = 1.f / l;
         __nv_bfloat16* op = a.out + (x.qs + x.q0 + t) * a.out_stride + (int64_t)seg.h * kPfHD;
 #pragma unroll
@@ -629,15 +644,71 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           w.w = pack_bf16x2(__uint_as_float(v[8 * c + 6]) * inv, __uint_as_float(v[8 * c + 7]) * inv);
           *reinterpret_cast<uint4*>(op + 8 * c) = w;
         }
-      } else if (t < x.nq) {
-        // partial of a segment cut by this CTA's range: slot 0 = the CTA's
-        // first segment, 1 = its last (d-major so that a warp's stores and the
-        // combine kernel's loads are contiguous)
-        float* ps = a.partials + ((int64_t)blockIdx.x * 2 + (k == 0 ? 0 : 1)) * kPfPartialFloats;
-        ps[t] = m_ref;
-        ps[kPfBM + t] = l;
+        }
+      } else if (tlo > 0) {
+        // the segment began in an earlier CTA's range (so it is this CTA's
+        // first segment): leave the partial (d-major, so that a warp's stores
+        // and the merging warp's loads are contiguous) and raise this warp's flag
+        float* ps = a.partials + (int64_t)blockIdx.x * kPfPartialFloats;
+        if (t < x.nq) {
+          ps[t] = m_ref;
+          ps[kPfBM + t] = l;
 #pragma unroll
-        for (int d = 0; d < kPfHD; ++d) ps[2 * kPfBM + d * kPfBM + t] = __uint_as_float(v[d]);
+          for (int d = 0; d < kPfHD; ++d) ps[2 * kPfBM + d * kPfBM + t] = __uint_as_float(v[d]);
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_gpu(a.flags + blockIdx.x * 4 + warp, 1);
+      } else {
+        // the segment begins here and continues into CTAs c+1 .. c1: wait for
+        // their partials of this warp's rows, merge in CTA order, write
+        const int64_t c1 = (seg.start + seg.n - 1) / W;
+        for (int64_t c = blockIdx.x + 1; ok && c <= c1; ++c) {
+          const int32_t* flag = a.flags + c * 4 + warp;
+          uint32_t i = 0;
+          while (ld_acquire_gpu(flag) == 0) {
+            if (++i == kPfMergeWait || ((i & 1023u) == 0 && *reinterpret_cast<volatile int*>(&b->abort))) {
+              if (i == kPfMergeWait) {
+                *reinterpret_cast<volatile int*>(&b->abort) = 1;
+                raise_flag(a.err, NIE_DEV_ERR_TIMEOUT);
+              }
+              ok = false;
+              break;
+            }
+          }
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        if (t < x.nq) {
+          float M = m_ref;
+          for (int64_t c = blockIdx.x + 1; c <= c1; ++c) M = fmaxf(M, a.partials[c * kPfPartialFloats + t]);
+          const float w0 = (m_ref == -INFINITY) ? 0.f : fast_exp2(m_ref - M);
+          float L = l * w0;
+#pragma unroll
+          for (int d = 0; d < kPfHD; ++d) v[d] = __float_as_uint(__uint_as_float(v[d]) * w0);
+          for (int64_t c = blockIdx.x + 1; c <= c1; ++c) {
+            const float* ps = a.partials + c * kPfPartialFloats;
+            const float m = ps[t];
+            const float w = (m == -INFINITY) ? 0.f : fast_exp2(m - M);
+            L += ps[kPfBM + t] * w;
+#pragma unroll
+            for (int d = 0; d < kPfHD; ++d)
+              v[d] = __float_as_uint(fmaf(ps[2 * kPfBM + d * kPfBM + t], w, __uint_as_float(v[d])));
+          }
+          const float inv = 1.f / L;
+          __nv_bfloat16* op = a.out + (x.qs + x.q0 + t) * a.out_stride + (int64_t)seg.h * kPfHD;
+#pragma unroll
+          for (int c = 0; c < kPfHD / 8; ++c) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(v[8 * c + 0]) * inv, __uint_as_float(v[8 * c + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(v[8 * c + 2]) * inv, __uint_as_float(v[8 * c + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(v[8 * c + 4]) * inv, __uint_as_float(v[8 * c + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(v[8 * c + 6]) * inv, __uint_as_float(v[8 * c + 7]) * inv);
+            *reinterpret_cast<uint4*>(op + 8 * c) = w;
+          }
+        }
       }
     }
   }
@@ -650,61 +721,11 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   }
 }
 
-// Merge the partials of segments that were cut across CTAs (stream mode).
-// grid = (units, q_heads, kPfCombineSplit), one thread per query row and
-// kPfHD / kPfCombineSplit head dimensions.  Launched as a dependent of the
-// attention kernel: it reads nothing before pdl_wait().
-constexpr int kPfCombineSplit = 4;
-constexpr int kPfCombineD = kPfHD / kPfCombineSplit;
-__global__ void __launch_bounds__(kPfBM) prefill_combine_kernel(PrefillArgs a) {
-  pdl_wait();
-  const int u = blockIdx.x, h = blockIdx.y, t = threadIdx.x, d0 = blockIdx.z * kPfCombineD;
-  const int32_t* cum = a.cum_out;
-  const int d = cum[u + 1] - cum[u];
-  const int64_t W = cum[kPfMaxUnits + 1];
-  if (d == 0 || W <= 0) return;
-  // the segment's cost interval starts at s0; its key tiles occupy [s1, s2)
-  const int64_t s0 = (int64_t)a.hq * cum[u] + (int64_t)h * d, s1 = s0 + kPfSegCost, s2 = s0 + d;
-  const int64_t c0 = s1 / W, c1 = (s2 - 1) / W;  // the CTAs that processed its tiles
-  if (c0 == c1) return;  // written directly by its CTA
-  const PfUnit x = pf_unit(a, u);
-  if (t >= x.nq) return;
-  // the partial of CTA c is in its slot 0 when the segment is c's first one
-  auto slot = [&](int64_t c) {
-    return a.partials + (c * 2 + (s0 <= c * W ? 0 : 1)) * kPfPartialFloats;
-  };
-  float M = -INFINITY;
-  for (int64_t c = c0; c <= c1; ++c) M = fmaxf(M, slot(c)[t]);
-  float L = 0.f;
-  float o[kPfCombineD];
-#pragma unroll
-  for (int j = 0; j < kPfCombineD; ++j) o[j] = 0.f;
-  for (int64_t c = c0; c <= c1; ++c) {
-    const float* ps = slot(c);
-    const float m = ps[t];
-    const float w = (m == -INFINITY) ? 0.f : fast_exp2(m - M);
-    L += ps[kPfBM + t] * w;
-#pragma unroll
-    for (int j = 0; j < kPfCombineD; ++j) o[j] += ps[2 * kPfBM + (d0 + j) * kPfBM + t] * w;
-  }
-  const float inv = 1.f / L;
-  __nv_bfloat16* op = a.out + (x.qs + x.q0 + t) * a.out_stride + (int64_t)h * kPfHD + d0;
-#pragma unroll
-  for (int c = 0; c < kPfCombineD / 8; ++c) {
-    uint4 w;
-    w.x = pack_bf16x2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
-    w.y = pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-    w.z = pack_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-    w.w = pack_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-    *reinterpret_cast<uint4*>(op + 8 * c) = w;
-  }
-}
-
 size_t prefill_workspace_bytes(int32_t num_requests, int32_t max_query_len, int32_t max_seq_len, int32_t q_heads) {
   (void)max_seq_len;
   (void)q_heads;
   if (num_requests <= 0 || max_query_len <= 0) return 0;
-  return kPfCumBytes + (size_t)kPfMaxCtas * 2 * kPfPartialFloats * sizeof(float);
+  return kPfFlagBytes + (size_t)kPfMaxCtas * kPfPartialFloats * sizeof(float);
 }
 
 static size_t prefill_smem_bytes() {
@@ -774,8 +795,8 @@ int launch_prefill_tc(const void* q, void* out, int64_t row_stride, int64_t num_
   const size_t need = prefill_workspace_bytes(num_requests, max_query_len, max_seq_len, q_heads);
   pa.stream = workspace != nullptr && workspace_bytes >= need && (reinterpret_cast<uintptr_t>(workspace) % 256) == 0;
   if (pa.stream) {
-    pa.cum_out = (int32_t*)workspace;
-    pa.partials = (float*)((char*)workspace + kPfCumBytes);
+    pa.flags = (int32_t*)workspace;
+    pa.partials = (float*)((char*)workspace + kPfFlagBytes);
   }
   pa.scale = scale;
   pa.scale_log2e = scale * kPfLog2e;
@@ -792,11 +813,10 @@ int launch_prefill_tc(const void* q, void* out, int64_t row_stride, int64_t num_
   } else {
     grid = (int)(units * q_heads);  // one segment per CTA
   }
+  if (pa.stream && cudaMemsetAsync(pa.flags, 0, kPfFlagBytes, s) != cudaSuccess)
+    return fail(NIE_ERR_CUDA, "cannot clear the prefill flags");
   prefill_tc_kernel<<<grid, kPfThreads, smem, s>>>(qmap, kmap, vmap, pa);
-  int rc = check_launch("prefill_tc_kernel");
-  if (rc != NIE_OK || !pa.stream) return rc;
-  pdl_launch(prefill_combine_kernel, dim3((unsigned)units, (unsigned)q_heads, kPfCombineSplit), dim3(kPfBM), s, pa);
-  return check_launch("prefill_combine_kernel");
+  return check_launch("prefill_tc_kernel");
 }
 
 }  // namespace nie

@@ -174,7 +174,7 @@ std::tuple<at::Tensor, int64_t> run_layers(
                                  (int32_t)max_seq_len, scale, var_bytes ? var_ws->data_ptr() : nullptr, var_bytes,
                                  err.data_ptr<int32_t>(), stream),
             "nie_varlen_attention");
-      launches += var_bytes ? 2 : 1;
+      launches += 1;
     }
     at::Tensor attn = linear(att.view({T, hidden}), o_w, /*overlap=*/true);  // after the attention kernels
     // h = attn + residual, normed2 = post-norm(h)

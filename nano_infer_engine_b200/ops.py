@@ -581,7 +581,7 @@ def varlen_attention(
         _stream(device),
     )
     check(status, "nie_varlen_attention")
-    _count(2 if need else 1)
+    _count()
     return out
 
 
