@@ -280,7 +280,10 @@ int nie_paged_decode_noalloc(const void* q, int64_t q_row_stride, void* out,
  * generic kernel.  max_seq_len (host value, >= every seq_lens[r]; 0 =
  * unknown) lets the tensor-core path split long key ranges over several CTAs;
  * the split needs `workspace` of nie_varlen_workspace_size() bytes (scratch,
- * no initialisation needed) and is skipped when it is NULL or too small.
+ * no initialisation needed: the call clears its flags on the stream) and is
+ * skipped when it is NULL or too small.  Split ranges are merged inside the
+ * one kernel: the call launches a memset and one kernel, and calls sharing a
+ * workspace must not overlap on the GPU.
  */
 size_t nie_varlen_workspace_size(int32_t num_requests, int32_t max_query_len,
                                  int32_t max_seq_len, int32_t q_heads);
