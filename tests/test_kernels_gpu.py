@@ -266,8 +266,9 @@ def test_varlen_against_oracle(cuda, dtype):
 def test_tensor_core_varlen_against_oracle(cuda, seed, contexts, qlens, split):
     """tcgen05 path (bf16, hd 64, bs 16): multi-tile queries, long contexts, ragged
     ends; stale rows past each sequence end hold NaN and must not leak.  With
-    ``split`` the key range of long requests is divided over CTAs (1024-key
-    chunks) and merged by the combine kernel."""
+    ``split`` (a workspace) the persistent grid cuts segments across CTAs and
+    merges their partials inside the kernel; without it each CTA takes one
+    whole segment."""
     g = torch.Generator().manual_seed(seed)
     bs, hkv, hq = 16, 8, 32
     lens = [c + q for c, q in zip(contexts, qlens)]
