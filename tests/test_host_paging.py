@@ -210,3 +210,20 @@ def test_layer_loop_eligibility_follows_the_python_loop_checks():
     attn = model.decoders[0].attn
     attn.k_proj.weight = nn.Parameter(attn.k_proj.weight.detach().clone())  # no longer a view of the fused buffer
     assert model._layer_loop_args(torch.bfloat16) is None
+
+
+def test_reserve_table_grows_once_and_never_shrinks():
+    from nano_infer_engine_b200.paged_cache import PagedKVCache
+
+    cache = PagedKVCache(64, 16, 1, 1, 4, torch.float32, "cpu")
+    rows, cols = cache._table_host.shape
+    cache.reserve_table(rows * 4, cols * 2)
+    assert cache._table_host.shape == (rows * 4, cols * 2)
+    cache.reserve_table(1, 1)  # smaller: nothing changes
+    assert cache._table_host.shape == (rows * 4, cols * 2)
+    # sequences keep their tables across a reservation
+    cache.ensure_capacity("a", 40)
+    before = cache.get_block_table("a")
+    cache.reserve_table(rows * 8, cols * 2)
+    assert cache.get_block_table("a") == before
+    assert cache._table_host[cache.table_row("a"), : len(before)].tolist() == list(before)
