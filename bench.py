@@ -353,6 +353,28 @@ def time_pd(pd, steps, warmup, dist_ctx, e2e=False):
     return max_over_ranks(dist_ctx, elapsed, pd.device), [int(x) for x in totals.tolist()]
 
 
+def pd_layout(args, world):
+    """(k, groups): decode ranks per prefill rank and P/D groups at N = world, the
+    rule both arms use (--pd-decode-per-prefill, else 3 when N is a multiple of 4,
+    else 1); groups = 0 when N does not form groups (replicas)."""
+    k = args.pd_decode_per_prefill if args.pd_decode_per_prefill is not None else (3 if world % 4 == 0 else 1)
+    return k, (world // (k + 1) if world >= 2 and k >= 1 and world % (k + 1) == 0 else 0)
+
+
+def pd_config(args, base, groups, k):
+    """The N >= 2 P/D workload description, shared verbatim by both arms."""
+    lens = [p.shape[1] for p in base]
+    return {
+        "workload": f"config5 P/D, closed loop: Llama-3.2-1B shape, the same {len(base)} requests per decode GPU "
+                    f"(prompts log-normal mean 1024 capped 8192, per decode GPU sum {sum(lens)}, max {max(lens)}), "
+                    f"{args.new_tokens} greedy new tokens; prefill batches <=4096 tokens in chunks <=2048; KV blocks "
+                    "pulled over NVLink by the decode GPU",
+        "global_batch": len(base) * groups * k,
+        "parallelism": f"{groups} P/D groups of 1 prefill + {k} decode ranks behind the router",
+        "l2": "inputs larger than L2 (2.47 GB of weights streamed per decode step)",
+    }
+
+
 def pd_job(decode_ranks, new_tokens):
     """The closed-loop job for ``decode_ranks`` decode GPUs: the same seeded
     32-request set (config 5's prompt-length distribution) for every decode
@@ -400,7 +422,6 @@ def run_pd(args, dist_ctx, rank, local, device, world):
                     "ms_per_launch": dec["ms"], "peak_kind": f"{peak_kind} (hbm_gbs burst copy)"}
     barrier(dist_ctx)
     if rank == 0:
-        lens = [p.shape[1] for p in base]
         print(json.dumps({
             "metric": METRIC,
             "value": value,
@@ -417,15 +438,7 @@ def run_pd(args, dist_ctx, rank, local, device, world):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded prompts, random-init weights N(0, 0.02))",
-            "config": {
-                "workload": f"config5 P/D, closed loop: Llama-3.2-1B shape, the same {len(base)} requests per decode GPU "
-                            f"(prompts log-normal mean 1024 capped 8192, per decode GPU sum {sum(lens)}, max {max(lens)}), "
-                            f"{args.new_tokens} greedy new tokens; prefill batches <=4096 tokens in chunks <=2048; KV blocks pulled "
-                            "over NVLink by the decode GPU",
-                "global_batch": len(host),
-                "parallelism": f"{groups} P/D groups of 1 prefill + {k} decode ranks behind the router",
-                "l2": "inputs larger than L2 (2.47 GB of weights streamed per decode step)",
-            },
+            "config": pd_config(args, base, groups, k),
             "roofline": roofline,
             "cpu_baseline": None,
             "e2e": e2e,
@@ -818,6 +831,44 @@ def cpu_sample(prompts, model_cpu_state, threads):
     return t_pf, t_dec
 
 
+def cpu_sample_pd(prompts, model_cpu_state, threads):
+    """The P/D job's reference algorithm (oracle port) on the host: the first
+    prefill batch of a decode GPU's requests (<= 4096 tokens, prompts in
+    chunks of <= 2048, as the prefill rank forms it) and one decode step of
+    all its requests at their prompt contexts.  Returns (seconds, tokens) of
+    the batch and the decode step's seconds."""
+    from oracle.engine import OracleCache, OracleLlama
+    from oracle.weights import LLAMA_1B
+
+    torch.set_num_threads(threads)
+    cfg = LLAMA_1B
+    model = OracleLlama(model_cpu_state, cfg)
+    lens = [p.shape[1] for p in prompts]
+    blocks = 2 * sum(-(-(n + 1) // 16) for n in lens) + 64
+    hd = cfg["hidden_size"] // cfg["q_head_num"]
+    cache = OracleCache(blocks, 16, cfg["num_layers"], cfg["kv_head_num"], hd, torch.bfloat16)
+    batch, chunks, tokens = [], [], 0
+    for i, n in enumerate(lens):
+        take = min(n, 2048, 4096 - tokens)
+        if take <= 0:
+            break
+        batch.append(f"p{i}")
+        chunks.append(take)
+        tokens += take
+    ids = [f"r{i}" for i in range(len(prompts))]
+    for s_, n in zip(ids, lens):  # decode contexts: every prompt cached (values do not affect time)
+        cache.tables.ensure_capacity(s_, n)
+        cache.tables.advance(s_, n)
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        model.forward_ragged(torch.randint(0, 128256, (tokens,)), batch, chunks, cache, last_only=True)
+        t_pf = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        model.forward_ragged(torch.randint(0, 128256, (len(ids),)), ids, [1] * len(ids), cache, last_only=True)
+        t_dec = time.perf_counter() - t0
+    return t_pf, tokens, t_dec
+
+
 def cpu_baseline(prompts, new_tokens, state):
     threads = os.cpu_count() or 1
     t_pf, t_dec = cpu_sample(prompts, state, threads)
@@ -875,23 +926,45 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", 0))
     if rank != 0:
         return 0
-    prompts = workload(args.requests)
     state = cpu_state_for_oracle()
     threads = os.cpu_count() or 1
+    k, groups = pd_layout(args, args.gpus)
+    if groups:
+        # the product arm's N >= 2 workload: the P/D closed loop, one host doing
+        # every decode GPU's share in turn (the rate does not depend on N)
+        prompts = pd_workload(2 * PD_REQUESTS_PER_GPU)
+        config = pd_config(args, prompts, groups, k)
+
+        def one_step():
+            t_pf, pf_tokens, t_dec = cpu_sample_pd(prompts, state, threads)
+            prefill_s = t_pf * sum(p.shape[1] for p in prompts) / pf_tokens
+            return len(prompts) * args.new_tokens / (prefill_s + args.new_tokens * t_dec)
+
+        sample = ("oracle port of the reference forward (torch on the host cores, no product code loaded); "
+                  "each step times one P/D prefill batch (<=4096 tokens, chunks <=2048) and one decode step of "
+                  f"the {len(prompts)} requests of a decode GPU at their prompt contexts and extrapolates to that "
+                  f"GPU's job (its prompt tokens + {args.new_tokens} decode steps); median over steps")
+    else:
+        prompts = workload(args.requests)
+        config = headline_config(args, max(1, args.gpus))
+
+        def one_step():
+            t_pf, t_dec = cpu_sample(prompts, state, threads)
+            n_pf = math.ceil(sum(p.shape[1] for p in prompts) / 512)
+            return len(prompts) * args.new_tokens / (n_pf * t_pf + args.new_tokens * t_dec)
+
+        sample = ("oracle port of the reference forward (torch on the host cores, no product code loaded); "
+                  "each step times one 512-token prefill step (4 chunks of 128) and one 16-request decode step "
+                  "at the workload's prompt contexts and extrapolates to the whole generation "
+                  f"(ceil(sum(prompt)/512) prefill + {args.new_tokens} decode steps); median over steps")
     for _ in range(args.warmup):
-        cpu_sample(prompts, state, threads)
+        one_step()
     values = []
     t_start = time.perf_counter()
     for _ in range(args.steps):
-        t_pf, t_dec = cpu_sample(prompts, state, threads)
-        n_pf = math.ceil(sum(p.shape[1] for p in prompts) / 512)
-        values.append(len(prompts) * args.new_tokens / (n_pf * t_pf + args.new_tokens * t_dec))
+        values.append(one_step())
     wall = time.perf_counter() - t_start
     value = statistics.median(values)
-    sample = ("oracle port of the reference forward (torch on the host cores, no product code loaded); "
-              "each step times one 512-token prefill step (4 chunks of 128) and one 16-request decode step "
-              "at the workload's prompt contexts and extrapolates to the whole generation "
-              f"(ceil(sum(prompt)/512) prefill + {args.new_tokens} decode steps); median over steps")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -906,7 +979,7 @@ def run_reference(args):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded prompts, random-init weights N(0, 0.02))",
-        "config": headline_config(args, 1),
+        "config": config,
         "sample": sample,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

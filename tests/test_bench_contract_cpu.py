@@ -10,13 +10,15 @@ import subprocess
 import sys
 from pathlib import Path
 
+import pytest
+
 ROOT = Path(__file__).resolve().parent.parent
 
 # Runs bench.py as __main__ and reports, after it returns, which product
 # modules and shared objects the process loaded.
 _PROBE = r"""
 import json, runpy, sys
-sys.argv = ["bench.py", "--impl", "reference", "--steps", "1", "--warmup", "1"]
+sys.argv = ["bench.py", "--impl", "reference", "--steps", "1", "--warmup", "1", "--gpus", GPUS]
 try:
     runpy.run_path("bench.py", run_name="__main__")
 except SystemExit as exc:
@@ -28,8 +30,10 @@ print("PROBE " + json.dumps({"modules": mods, "libs": libs}))
 """
 
 
-def test_reference_arm_prints_the_contract_line():
-    proc = subprocess.run([sys.executable, "-c", _PROBE], capture_output=True, text=True, timeout=600, cwd=ROOT)
+@pytest.mark.parametrize("gpus", [1, 2])
+def test_reference_arm_prints_the_contract_line(gpus):
+    probe_src = _PROBE.replace("GPUS", repr(str(gpus)))
+    proc = subprocess.run([sys.executable, "-c", probe_src], capture_output=True, text=True, timeout=600, cwd=ROOT)
     assert proc.returncode == 0, proc.stderr[-2000:]
     lines = proc.stdout.splitlines()
     out = json.loads([l for l in lines if l.startswith("{")][-1])
@@ -49,8 +53,13 @@ def test_reference_arm_prints_the_contract_line():
 
     import bench
 
-    args = argparse.Namespace(requests=16)
-    assert out["config"] == bench.headline_config(args, 1)
+    if gpus == 1:
+        assert out["config"] == bench.headline_config(argparse.Namespace(requests=16), 1)
+    else:  # the product arm's P/D workload (one pair at N=2), sampled on the host
+        args = argparse.Namespace(new_tokens=256, pd_decode_per_prefill=None)
+        k, groups = bench.pd_layout(args, gpus)
+        assert (k, groups) == (1, 1)
+        assert out["config"] == bench.pd_config(args, bench.pd_workload(2 * bench.PD_REQUESTS_PER_GPU), groups, k)
 
 
 def test_oracle_weights_equal_the_engine_init():
