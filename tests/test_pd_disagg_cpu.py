@@ -371,3 +371,24 @@ def test_group_router_gives_each_decode_rank_one_copy_of_a_replicated_job():
         for group in out:
             for slot in group:
                 assert sorted(job[i] for i in slot) == sorted(base)
+
+
+def test_run_prefill_route_is_checked_before_any_work():
+    cache = PagedKVCache(8, 4, 1, 1, 4, torch.float32, "cpu")
+    prompts = [(0, torch.zeros(1, 3, dtype=torch.long)), (1, torch.zeros(1, 2, dtype=torch.long))]
+    with pytest.raises(ValueError, match="route is required"):
+        run_prefill(None, cache, [_LoopbackChannel(), _LoopbackChannel()], prompts)
+    with pytest.raises(ValueError, match="route must name"):
+        run_prefill(None, cache, [_LoopbackChannel(), _LoopbackChannel()], prompts, route=[0, 2])
+    with pytest.raises(ValueError, match="route must name"):
+        run_prefill(None, cache, [_LoopbackChannel(), _LoopbackChannel()], prompts, route=[0])
+    assert cache.allocator.free_block_count == 8
+
+
+def test_assign_groups_with_one_decode_rank_is_the_pair_router():
+    from nano_infer_engine_b200.generation.pd_disagg import assign_groups
+
+    rng = torch.Generator().manual_seed(3)
+    work = torch.randint(1, 500, (57,), generator=rng).tolist()
+    for groups in (1, 2, 3, 5):
+        assert [g[0] for g in assign_groups(work, groups, 1)] == assign_pairs(work, groups)
